@@ -1,0 +1,177 @@
+"""GPU parity of the Page16 decode kernel (libbpkv.so) against the oracle.
+
+Tolerances (from the spec of this path): fp32 inputs max-abs 1e-5 against an
+fp64 restatement; bf16 / fp16 inputs max-abs 2e-3 against the fp32/fp64
+restatement of the same (rounded) inputs.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.page16 import page16_decode_reference
+from tests.golden.inputs import PAGE16_CASES, page16_case
+
+pytestmark = pytest.mark.gpu
+GOLDEN = __import__("pathlib").Path(__file__).parent / "golden"
+TOL = {torch.float32: 1e-5, torch.float16: 2e-3, torch.bfloat16: 2e-3}
+
+
+def _run(cuda, q, k, v, bt, lens, dtype, scale=None, lse=False, layer_view=False):
+    from unifiedkv_b200.page16_native import page16_decode_attention
+    d = q.shape[-1]
+    scale = scale if scale is not None else 1.0 / math.sqrt(d)
+    tq = torch.from_numpy(np.asarray(q, np.float32)).to(cuda, dtype)
+    tk = torch.from_numpy(np.asarray(k, np.float32)).to(cuda, dtype)
+    tv = torch.from_numpy(np.asarray(v, np.float32)).to(cuda, dtype)
+    if layer_view:  # exercise a non-zero layer of a [L, N, 16, h, d] pool
+        pool_k = torch.zeros((3,) + tuple(tk.shape), dtype=dtype, device=cuda)
+        pool_v = torch.zeros_like(pool_k)
+        pool_k[1].copy_(tk)
+        pool_v[1].copy_(tv)
+        tk, tv = pool_k[1], pool_v[1]
+    lse_t = torch.empty(q.shape[0], q.shape[1], dtype=torch.float32, device=cuda) if lse else None
+    out = page16_decode_attention(tq, tk, tv, torch.from_numpy(bt).to(cuda), torch.from_numpy(lens).to(cuda),
+                                  softmax_scale=scale, n_rep=q.shape[1] // k.shape[2], lse_out=lse_t)
+    torch.cuda.synchronize()
+    # oracle sees exactly the rounded inputs the kernel saw
+    qr, kr, vr = (t.float().cpu().numpy() for t in (tq, tk, tv))
+    return out.float().cpu().numpy(), (lse_t.cpu().numpy() if lse else None), (qr, kr, vr)
+
+
+@pytest.mark.parametrize("name", sorted(PAGE16_CASES))
+def test_golden_cases(cuda, name):
+    cfg = PAGE16_CASES[name]
+    q, k, v, bt, lens = page16_case(**cfg)
+    dtype = torch.float32 if q.dtype == np.float32 else torch.float16
+    out, _, (qr, kr, vr) = _run(cuda, q, k, v, bt, lens, dtype)
+    g = np.load(GOLDEN / f"page16_{name}.npz")
+    ref = page16_decode_reference(qr, kr, vr, bt, lens, float(g["scale"]), int(g["n_rep"]))
+    assert np.max(np.abs(out - ref)) < TOL[dtype]
+    # and against the reference kernel's own output
+    assert np.max(np.abs(out - g["out"])) < (1e-5 if dtype == torch.float32 else 2e-3)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (8, 2, 64), (16, 1, 128), (8, 8, 128), (8, 4, 256),
+                                      (12, 3, 96), (40, 2, 64)])
+def test_shapes_and_dtypes(cuda, dtype, hq, hkv, d):
+    lens = (1, 15, 16, 17, 129, 700, 2049)
+    q, k, v, bt, lens = page16_case(seed=hq * 7 + d, batch=len(lens), hq=hq, hkv=hkv, d=d, lens=lens,
+                                    num_pages=300, scale_std=0.5)
+    out, lse, (qr, kr, vr) = _run(cuda, q, k, v, bt, lens, dtype, lse=True)
+    ref, ref_lse = page16_decode_reference(qr, kr, vr, bt, lens, 1 / math.sqrt(d), hq // hkv, return_lse=True)
+    assert np.max(np.abs(out - ref)) < TOL[dtype]
+    assert np.max(np.abs(lse - ref_lse)) < 1e-3
+
+
+def test_empty_and_capped_lengths(cuda):
+    # len 0 -> NaN row (reference 0/0); len beyond 16*max_blocks reads max_blocks pages only
+    q, k, v, bt, lens = page16_case(seed=31, batch=4, hq=8, hkv=2, d=128, lens=(0, 40, 1000, 3),
+                                    num_pages=100, max_blocks=20, scale_std=0.5)
+    out, _, (qr, kr, vr) = _run(cuda, q, k, v, bt, lens, torch.bfloat16)
+    ref = page16_decode_reference(qr, kr, vr, bt, lens, 1 / math.sqrt(128), 4)
+    assert np.isnan(out[0]).all()
+    assert np.isfinite(out[1:]).all()
+    assert np.max(np.abs(out[1:] - ref[1:])) < 2e-3
+
+
+def test_layer_view_and_stale_pages(cuda):
+    # pages past len hold NaN: must not leak into the output (reference masks them)
+    q, k, v, bt, lens = page16_case(seed=32, batch=3, hq=16, hkv=4, d=128, lens=(33, 250, 17),
+                                    num_pages=64, scale_std=0.5)
+    k = k.copy(); v = v.copy()
+    for b, l in enumerate(lens):
+        last = bt[b, (l - 1) // 16]
+        k[last, l % 16 or 16:] = np.nan
+        v[last, l % 16 or 16:] = np.nan
+    out, _, (qr, kr, vr) = _run(cuda, q, k, v, bt, lens, torch.bfloat16, layer_view=True)
+    ref = page16_decode_reference(qr, kr, vr, bt, lens, 1 / math.sqrt(128), 4)
+    assert np.isfinite(out).all()
+    assert np.max(np.abs(out - ref)) < 2e-3
+
+
+def test_llama8b_decode_layer_sampled(cuda):
+    """Config 2 shapes (one layer): B=32, 32/8 heads, d=128, ctx U[4096,32768], bf16, q/k/v ~ 0.5 N(0,1)."""
+    from unifiedkv_b200.page16_native import page16_decode_attention
+    rng = np.random.default_rng(2)
+    B, hq, hkv, d = 32, 32, 8, 128
+    lens = rng.integers(4096, 32769, size=B).astype(np.int32)
+    need = (lens + 15) // 16
+    n_pages = int(need.sum()) + 64
+    g = torch.Generator(device=cuda).manual_seed(2)
+    kc = (torch.randn((n_pages, 16, hkv, d), generator=g, device=cuda) * 0.5).to(torch.bfloat16)
+    vc = (torch.randn((n_pages, 16, hkv, d), generator=g, device=cuda) * 0.5).to(torch.bfloat16)
+    q = (torch.randn((B, hq, d), generator=g, device=cuda) * 0.5).to(torch.bfloat16)
+    perm = rng.permutation(n_pages).astype(np.int32)
+    mb = int(need.max())
+    bt = np.zeros((B, mb), np.int32)
+    off = 0
+    for b in range(B):
+        bt[b, :need[b]] = perm[off:off + need[b]]
+        off += need[b]
+    out = page16_decode_attention(q, kc, vc, torch.from_numpy(bt).to(cuda), torch.from_numpy(lens).to(cuda),
+                                  softmax_scale=d ** -0.5, n_rep=4)
+    out2 = page16_decode_attention(q, kc, vc, torch.from_numpy(bt).to(cuda), torch.from_numpy(lens).to(cuda),
+                                   softmax_scale=d ** -0.5, n_rep=4)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2), "decode must be deterministic"
+    for b in [0, 7, 19, 31]:
+        ids = torch.from_numpy(bt[b, :need[b]].astype(np.int64)).to(cuda)
+        kb = kc.index_select(0, ids).float().cpu().numpy()
+        vb = vc.index_select(0, ids).float().cpu().numpy()
+        ref = page16_decode_reference(q[b:b + 1].float().cpu().numpy(), kb, vb,
+                                      np.arange(need[b], dtype=np.int32)[None], lens[b:b + 1], d ** -0.5, 4,
+                                      compute_dtype=np.float32)
+        assert np.max(np.abs(out[b:b + 1].float().cpu().numpy() - ref)) < 2e-3
+
+
+def test_single_sequence_131k(cuda):
+    """Config 3 shapes: one request of 131072 tokens (8192 pages), 32/8 heads, bf16."""
+    from unifiedkv_b200.page16_native import page16_decode_attention
+    d, hq, hkv, L = 128, 32, 8, 131072
+    g = torch.Generator(device=cuda).manual_seed(3)
+    n_pages = L // 16
+    kc = torch.randn((n_pages, 16, hkv, d), generator=g, device=cuda).to(torch.bfloat16)
+    vc = torch.randn((n_pages, 16, hkv, d), generator=g, device=cuda).to(torch.bfloat16)
+    q = (torch.randn((1, hq, d), generator=g, device=cuda) * 0.5).to(torch.bfloat16)
+    bt = torch.randperm(n_pages, generator=g, device=cuda).to(torch.int32)[None]
+    lens = torch.tensor([L], dtype=torch.int32, device=cuda)
+    out = page16_decode_attention(q, kc, vc, bt, lens, softmax_scale=d ** -0.5, n_rep=4)
+    ids = bt[0].long()
+    ref = page16_decode_reference(q.float().cpu().numpy(), kc.index_select(0, ids).float().cpu().numpy(),
+                                  vc.index_select(0, ids).float().cpu().numpy(),
+                                  np.arange(n_pages, dtype=np.int32)[None], np.array([L], np.int32), d ** -0.5, 4,
+                                  compute_dtype=np.float32)
+    assert np.max(np.abs(out.float().cpu().numpy() - ref)) < 2e-3
+
+
+def test_decode_append_then_decode(cuda):
+    from unifiedkv_b200.page16_native import decode_append
+    q, k, v, bt, lens = page16_case(seed=40, batch=3, hq=8, hkv=2, d=64, lens=(15, 16, 40), num_pages=20,
+                                    max_blocks=4, scale_std=0.5)
+    tk = torch.from_numpy(k).to(cuda, torch.bfloat16)
+    tv = torch.from_numpy(v).to(cuda, torch.bfloat16)
+    knew = torch.randn(3, 2, 64, device=cuda).to(torch.bfloat16)
+    vnew = torch.randn(3, 2, 64, device=cuda).to(torch.bfloat16)
+    tbt = torch.from_numpy(bt).to(cuda)
+    decode_append(knew, vnew, tk, tv, tbt, torch.from_numpy(lens).to(cuda))
+    torch.cuda.synchronize()
+    for b, l in enumerate(lens):
+        page = bt[b, l // 16]
+        assert torch.equal(tk[page, l % 16], knew[b]) and torch.equal(tv[page, l % 16], vnew[b])
+
+
+def test_shape_errors_use_reference_tokens(cuda):
+    from unifiedkv_b200.page16_native import page16_decode_attention
+    q = torch.zeros(2, 6, 64, device=cuda, dtype=torch.bfloat16)
+    kc = torch.zeros(4, 16, 4, 64, device=cuda, dtype=torch.bfloat16)
+    bt = torch.zeros(2, 2, dtype=torch.int32, device=cuda)
+    lens = torch.ones(2, dtype=torch.int32, device=cuda)
+    with pytest.raises(RuntimeError, match="page16_native_shape_unsupported:gqa"):
+        page16_decode_attention(q, kc, kc, bt, lens, softmax_scale=0.1, n_rep=1)
+    with pytest.raises(RuntimeError, match="page16_native_shape_unsupported:block_size_8"):
+        page16_decode_attention(q, kc[:, :8], kc[:, :8], bt, lens, softmax_scale=0.1, n_rep=1)
+    with pytest.raises(RuntimeError, match="page16_native_shape_unsupported:block_table_batch"):
+        page16_decode_attention(q[:, :4], kc, kc, bt[:1], lens, softmax_scale=0.1, n_rep=1)

@@ -1,0 +1,757 @@
+// Page16 split-KV GQA decode attention over the 16-token paged pool (sm_100a).
+//
+// Replaces the reference Triton kernel _page16_decode_kernel
+// (core/page16_native.py:17-80), which runs one program per (request, q-head),
+// walks every page serially and re-reads K/V once per q-head of a GQA group.
+//
+// Design (B200):
+//  * Work split.  All requests' pages form one flattened list of
+//    T = sum_b ceil(len_b/16) pages.  CTA c of G persistent CTAs owns pages
+//    [floor(cT/G), floor((c+1)T/G)) - every SM gets the same number of pages
+//    whatever the length mix.  A request cut by a range boundary yields one
+//    partial (o, lse) per owning CTA in workspace slot (c + b) (unique, because
+//    ranges are ordered), merged by a log-sum-exp combine kernel.
+//  * One warp per KV head.  Each warp streams its head's 16-row K and V tiles
+//    (16 x head_dim each) of every page through an NS-stage cp.async ring with
+//    16-byte zero-filling copies (rows past len are zero, so stale pool data
+//    never reaches the math), XOR-swizzled so ldmatrix is conflict free.
+//    Warps never wait on each other: no block barrier in the main loop.
+//  * All n_rep query heads of the group share one K/V read: S = Q_g K^T and
+//    O += P V run on mma.m16n8k16 (fp32 accumulate) with the n_rep heads as
+//    the M rows; P is reused straight from the S accumulators as the A
+//    fragment.  Online softmax in the exp2 domain, row max / sum by quad
+//    shuffles.
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace bpkv {
+namespace {
+
+struct DecodeParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int32_t* bt;
+  const int32_t* lens;
+  void* out;
+  float* lse_out;
+  int32_t* g_prefix;  // workspace: prefix[B+1] written by CTA (0,0)
+  float* part_lse;    // workspace: [slots][Hq]
+  float* part_o;      // workspace: [slots][Hq][D]
+  int B, Hq, Hkv, D, max_blocks, n_rep;
+  int64_t q_sb, q_sh, page_stride, bt_sb;
+  float scale;        // softmax scale
+  float scale_log2;   // softmax scale * log2(e)
+};
+
+constexpr float kLn2 = 0.6931471805599453f;
+
+__device__ __forceinline__ int npages_of(const DecodeParams& p, int b) {
+  int len = __ldg(p.lens + b);
+  if (len <= 0) return 0;
+  int np = (len + kPage - 1) / kPage;
+  return np < p.max_blocks ? np : p.max_blocks;
+}
+
+__device__ __forceinline__ int eff_len(const DecodeParams& p, int b) {
+  int len = __ldg(p.lens + b);
+  int cap = p.max_blocks * kPage;
+  return len < cap ? len : cap;
+}
+
+// Block-wide exclusive scan of per-request page counts into prefix[0..B].
+__device__ void build_prefix(const DecodeParams& p, int* prefix) {
+  __shared__ int wsum[32];
+  const int nt = blockDim.x, tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5, nw = (nt + 31) >> 5;
+  const int per = (p.B + nt - 1) / nt;
+  const int beg = tid * per;
+  const int end = min(beg + per, p.B);
+  int local = 0;
+  for (int i = beg; i < end; ++i) local += npages_of(p, i);
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nw ? wsum[lane] : 0;
+    int wi = w;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    wsum[lane] = wi - w;
+    if (lane == 31) prefix[p.B] = wi;
+  }
+  __syncthreads();
+  int run = wsum[warp] + incl - local;
+  for (int i = beg; i < end; ++i) {
+    prefix[i] = run;
+    run += npages_of(p, i);
+  }
+  __syncthreads();
+}
+
+// Largest b with prefix[b] <= s  (s < prefix[B]).
+__device__ __forceinline__ int find_request(const int* prefix, int B, int64_t s) {
+  int lo = 0, hi = B;  // invariant prefix[lo] <= s < prefix[hi]
+  while (hi - lo > 1) {
+    int mid = (lo + hi) >> 1;
+    if (prefix[mid] <= s) lo = mid; else hi = mid;
+  }
+  return lo;
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core kernel: bf16 / fp16, head_dim in {64,128,256}, n_rep <= 16.
+// ---------------------------------------------------------------------------
+template <typename T, int D, int NW, int NS>
+__global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  constexpr int ROWB = D * 2;       // bytes of one token row of one head
+  constexpr int TILEB = 16 * ROWB;  // one page, one head, K (or V)
+  constexpr int STAGEB = 2 * TILEB;
+  constexpr int CH = D / 8;                  // 16-byte chunks per row
+  constexpr int PER_LANE = 16 * CH / 32;     // chunks per lane per tile
+  constexpr int KS = D / 16;                 // mma k-steps over head_dim
+  constexpr int NT = D / 8;                  // 8-wide output column tiles
+
+  int* prefix = reinterpret_cast<int*>(smem + NW * NS * STAGEB);
+  build_prefix(p, prefix);
+  const int B = p.B;
+  const int64_t total = prefix[B];
+  const int G = gridDim.x, c = blockIdx.x;
+  if (c == 0 && blockIdx.y == 0) {
+    for (int i = threadIdx.x; i <= B; i += blockDim.x) p.g_prefix[i] = prefix[i];
+  }
+  if (total == 0) return;
+  const int64_t s = range_start(c, total, G), e = range_start(c + 1, total, G);
+  if (s >= e) return;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y * NW + warp;  // kv head of this warp
+  if (h >= p.Hkv) return;
+
+  const T* __restrict__ kg = reinterpret_cast<const T*>(p.k);
+  const T* __restrict__ vg = reinterpret_cast<const T*>(p.v);
+  const uint32_t ring = smem_u32(smem + warp * NS * STAGEB);
+  const int g = lane >> 2, cq = lane & 3;
+
+  // ---- loader ------------------------------------------------------------
+  auto issue = [&](int64_t fp, int b, int stage) {
+    const int j = static_cast<int>(fp - prefix[b]);
+    const int page = __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + j);
+    const int valid_rows = eff_len(p, b) - j * kPage;  // >= 1
+    const int64_t base = static_cast<int64_t>(page) * p.page_stride + static_cast<int64_t>(h) * D;
+    const uint32_t sk = ring + stage * STAGEB;
+    const uint32_t sv = sk + TILEB;
+#pragma unroll
+    for (int r = 0; r < PER_LANE; ++r) {
+      const int ci = lane + 32 * r;
+      const int tok = ci / CH, ch = ci % CH;
+      const bool ok = tok < valid_rows;
+      const int64_t off = base + static_cast<int64_t>(tok) * p.Hkv * D + ch * 8;
+      const uint32_t so = tok * ROWB + ((ch ^ (tok & 7)) << 4);
+      cp_async16(sk + so, ok ? (const void*)(kg + off) : (const void*)kg, ok);
+      cp_async16(sv + so, ok ? (const void*)(vg + off) : (const void*)vg, ok);
+    }
+  };
+
+  int b0 = find_request(prefix, B, s);
+  int64_t ld_p = s;
+  int ld_b = b0;
+#pragma unroll
+  for (int i = 0; i < NS - 1; ++i) {
+    if (ld_p < e) {
+      while (prefix[ld_b + 1] <= ld_p) ++ld_b;
+      issue(ld_p, ld_b, i);
+      ++ld_p;
+    }
+    cp_async_commit();
+  }
+
+  // ---- per-request state -------------------------------------------------
+  uint32_t qa[KS][4];
+  float acc[NT][4];
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+  int cur_b = -1, cur_len = 0;
+  int64_t seg_first = 0;
+  const int row0 = g, row1 = g + 8;
+  const bool r0ok = row0 < p.n_rep, r1ok = row1 < p.n_rep;
+
+  auto load_q = [&](int b) {
+    const T* qb = reinterpret_cast<const T*>(p.q) + static_cast<int64_t>(b) * p.q_sb;
+    const T* q0 = qb + static_cast<int64_t>(h * p.n_rep + row0) * p.q_sh;
+    const T* q1 = qb + static_cast<int64_t>(h * p.n_rep + row1) * p.q_sh;
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks) {
+      const int col = ks * 16 + 2 * cq;
+      qa[ks][0] = r0ok ? *reinterpret_cast<const uint32_t*>(q0 + col) : 0u;
+      qa[ks][1] = r1ok ? *reinterpret_cast<const uint32_t*>(q1 + col) : 0u;
+      qa[ks][2] = r0ok ? *reinterpret_cast<const uint32_t*>(q0 + col + 8) : 0u;
+      qa[ks][3] = r1ok ? *reinterpret_cast<const uint32_t*>(q1 + col + 8) : 0u;
+    }
+  };
+
+  auto finish = [&](int b, int64_t seg_end) {
+    float L0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+    L0 += __shfl_xor_sync(0xffffffffu, L0, 2);
+    float L1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+    L1 += __shfl_xor_sync(0xffffffffu, L1, 2);
+    const float inv0 = 1.f / L0, inv1 = 1.f / L1;
+    const float lse0 = (m0 + __log2f(L0)) * kLn2;
+    const float lse1 = (m1 + __log2f(L1)) * kLn2;
+    const bool whole = seg_first == prefix[b] && seg_end == prefix[b + 1];
+    const int hq0 = h * p.n_rep + row0, hq1 = h * p.n_rep + row1;
+    if (whole) {
+      T* ob = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(b) * p.Hq * D;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int col = n * 8 + 2 * cq;
+        if (r0ok)
+          *reinterpret_cast<uint32_t*>(ob + static_cast<int64_t>(hq0) * D + col) =
+              pack2<T>(acc[n][0] * inv0, acc[n][1] * inv0);
+        if (r1ok)
+          *reinterpret_cast<uint32_t*>(ob + static_cast<int64_t>(hq1) * D + col) =
+              pack2<T>(acc[n][2] * inv1, acc[n][3] * inv1);
+      }
+      if (p.lse_out != nullptr && cq == 0) {
+        if (r0ok) p.lse_out[static_cast<int64_t>(b) * p.Hq + hq0] = lse0;
+        if (r1ok) p.lse_out[static_cast<int64_t>(b) * p.Hq + hq1] = lse1;
+      }
+    } else {
+      const int64_t slot = static_cast<int64_t>(blockIdx.x) + b;
+      float* po = p.part_o + slot * p.Hq * D;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        const int col = n * 8 + 2 * cq;
+        if (r0ok)
+          *reinterpret_cast<float2*>(po + static_cast<int64_t>(hq0) * D + col) =
+              make_float2(acc[n][0] * inv0, acc[n][1] * inv0);
+        if (r1ok)
+          *reinterpret_cast<float2*>(po + static_cast<int64_t>(hq1) * D + col) =
+              make_float2(acc[n][2] * inv1, acc[n][3] * inv1);
+      }
+      if (cq == 0) {
+        if (r0ok) p.part_lse[slot * p.Hq + hq0] = lse0;
+        if (r1ok) p.part_lse[slot * p.Hq + hq1] = lse1;
+      }
+    }
+  };
+
+  int cb = b0;
+  for (int64_t fp = s; fp < e; ++fp) {
+    const int it = static_cast<int>(fp - s);
+    if (ld_p < e) {
+      while (prefix[ld_b + 1] <= ld_p) ++ld_b;
+      issue(ld_p, ld_b, (it + NS - 1) % NS);
+      ++ld_p;
+    }
+    cp_async_commit();
+
+    while (prefix[cb + 1] <= fp) ++cb;
+    if (cb != cur_b) {
+      if (cur_b >= 0) finish(cur_b, fp);
+      cur_b = cb;
+      cur_len = eff_len(p, cb);
+      seg_first = fp;
+      load_q(cb);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+      m0 = m1 = -INFINITY;
+      l0 = l1 = 0.f;
+    }
+
+    cp_async_wait<NS - 1>();
+    __syncwarp();
+
+    const uint32_t sk = ring + (it % NS) * STAGEB;
+    const uint32_t sv = sk + TILEB;
+    // ---- S = Q K^T  (rows: q heads, cols: 16 tokens as two n-tiles) ----
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int tok = rr + 8 * (mi >> 1);
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks) {
+        const int ch = 2 * ks + (mi & 1);
+        uint32_t b0r, b1r, b2r, b3r;
+        ldmatrix_x4(sk + tok * ROWB + ((ch ^ rr) << 4), b0r, b1r, b2r, b3r);
+        mma16816<T>(s0, qa[ks], b0r, b1r);
+        mma16816<T>(s1, qa[ks], b2r, b3r);
+      }
+    }
+    // ---- online softmax (log2 domain) ----
+    const int tbase = static_cast<int>(fp - prefix[cb]) * kPage;
+    const int t0 = tbase + 2 * cq, t1 = t0 + 8;
+    float x[8];
+    x[0] = (t0 < cur_len) ? s0[0] * p.scale_log2 : -INFINITY;
+    x[1] = (t0 + 1 < cur_len) ? s0[1] * p.scale_log2 : -INFINITY;
+    x[2] = (t0 < cur_len) ? s0[2] * p.scale_log2 : -INFINITY;
+    x[3] = (t0 + 1 < cur_len) ? s0[3] * p.scale_log2 : -INFINITY;
+    x[4] = (t1 < cur_len) ? s1[0] * p.scale_log2 : -INFINITY;
+    x[5] = (t1 + 1 < cur_len) ? s1[1] * p.scale_log2 : -INFINITY;
+    x[6] = (t1 < cur_len) ? s1[2] * p.scale_log2 : -INFINITY;
+    x[7] = (t1 + 1 < cur_len) ? s1[3] * p.scale_log2 : -INFINITY;
+    float mx0 = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[4], x[5]));
+    float mx1 = fmaxf(fmaxf(x[2], x[3]), fmaxf(x[6], x[7]));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float a0 = fast_exp2(m0 - mn0), a1 = fast_exp2(m1 - mn1);
+    m0 = mn0;
+    m1 = mn1;
+    float pr[8];
+    pr[0] = fast_exp2(x[0] - mn0);
+    pr[1] = fast_exp2(x[1] - mn0);
+    pr[2] = fast_exp2(x[2] - mn1);
+    pr[3] = fast_exp2(x[3] - mn1);
+    pr[4] = fast_exp2(x[4] - mn0);
+    pr[5] = fast_exp2(x[5] - mn0);
+    pr[6] = fast_exp2(x[6] - mn1);
+    pr[7] = fast_exp2(x[7] - mn1);
+    l0 = l0 * a0 + (pr[0] + pr[1] + pr[4] + pr[5]);
+    l1 = l1 * a1 + (pr[2] + pr[3] + pr[6] + pr[7]);
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      acc[n][0] *= a0;
+      acc[n][1] *= a0;
+      acc[n][2] *= a1;
+      acc[n][3] *= a1;
+    }
+    uint32_t pa[4];
+    pa[0] = pack2<T>(pr[0], pr[1]);
+    pa[1] = pack2<T>(pr[2], pr[3]);
+    pa[2] = pack2<T>(pr[4], pr[5]);
+    pa[3] = pack2<T>(pr[6], pr[7]);
+    // ---- O += P V ----
+    {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int tok = rr + 8 * (mi & 1);
+#pragma unroll
+      for (int dt = 0; dt < D / 16; ++dt) {
+        const int ch = 2 * dt + (mi >> 1);
+        uint32_t b0r, b1r, b2r, b3r;
+        ldmatrix_x4_trans(sv + tok * ROWB + ((ch ^ rr) << 4), b0r, b1r, b2r, b3r);
+        mma16816<T>(acc[2 * dt], pa, b0r, b1r);
+        mma16816<T>(acc[2 * dt + 1], pa, b2r, b3r);
+      }
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+  if (cur_b >= 0) finish(cur_b, e);
+}
+
+// ---------------------------------------------------------------------------
+// Generic CUDA-core kernel: any dtype (fp32 included), head_dim <= 256, any
+// GQA ratio.  Same work split and partial slots as the tensor-core kernel.
+// One warp per query head at a time; fp32 math with accurate expf.
+// ---------------------------------------------------------------------------
+template <typename T, int NW>
+__global__ void __launch_bounds__(NW * 32) page16_decode_generic_kernel(DecodeParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  int* prefix = reinterpret_cast<int*>(smem);
+  build_prefix(p, prefix);
+  const int B = p.B;
+  const int64_t total = prefix[B];
+  const int G = gridDim.x, c = blockIdx.x;
+  if (c == 0) {
+    for (int i = threadIdx.x; i <= B; i += blockDim.x) p.g_prefix[i] = prefix[i];
+  }
+  if (total == 0) return;
+  const int64_t s = range_start(c, total, G), e = range_start(c + 1, total, G);
+  if (s >= e) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int D = p.D;
+  const int nd = (D + 31) / 32;
+  const T* kg = reinterpret_cast<const T*>(p.k);
+  const T* vg = reinterpret_cast<const T*>(p.v);
+  const int b0 = find_request(prefix, B, s);
+
+  for (int hq = warp; hq < p.Hq; hq += NW) {
+    const int h = hq / p.n_rep;
+    float qv[8], acc[8];
+    float m = -INFINITY, l = 0.f;
+    int cur_b = -1, cur_len = 0;
+    int64_t seg_first = 0;
+    auto finish = [&](int b, int64_t seg_end) {
+      const bool whole = seg_first == prefix[b] && seg_end == prefix[b + 1];
+      const float inv = 1.f / l;
+      const float lse = m + logf(l);
+      if (whole) {
+        T* ob = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.Hq + hq) * D;
+        for (int i = 0; i < nd; ++i) {
+          const int d = lane + 32 * i;
+          if (d < D) ob[d] = Elem<T>::from_f(acc[i] * inv);
+        }
+        if (p.lse_out != nullptr && lane == 0) p.lse_out[static_cast<int64_t>(b) * p.Hq + hq] = lse;
+      } else {
+        const int64_t slot = static_cast<int64_t>(blockIdx.x) + b;
+        float* po = p.part_o + (slot * p.Hq + hq) * D;
+        for (int i = 0; i < nd; ++i) {
+          const int d = lane + 32 * i;
+          if (d < D) po[d] = acc[i] * inv;
+        }
+        if (lane == 0) p.part_lse[slot * p.Hq + hq] = lse;
+      }
+    };
+    int cb = b0;
+    for (int64_t fp = s; fp < e; ++fp) {
+      while (prefix[cb + 1] <= fp) ++cb;
+      if (cb != cur_b) {
+        if (cur_b >= 0) finish(cur_b, fp);
+        cur_b = cb;
+        cur_len = eff_len(p, cb);
+        seg_first = fp;
+        const T* qr = reinterpret_cast<const T*>(p.q) + static_cast<int64_t>(cb) * p.q_sb +
+                      static_cast<int64_t>(hq) * p.q_sh;
+        for (int i = 0; i < 8; ++i) {
+          const int d = lane + 32 * i;
+          qv[i] = (i < nd && d < D) ? Elem<T>::to_f(qr[d]) : 0.f;
+          acc[i] = 0.f;
+        }
+        m = -INFINITY;
+        l = 0.f;
+      }
+      const int j = static_cast<int>(fp - prefix[cb]);
+      const int page = __ldg(p.bt + static_cast<int64_t>(cb) * p.bt_sb + j);
+      const int rows = min(kPage, cur_len - j * kPage);
+      for (int t = 0; t < rows; ++t) {
+        const int64_t off = static_cast<int64_t>(page) * p.page_stride +
+                            (static_cast<int64_t>(t) * p.Hkv + h) * D;
+        float dot = 0.f;
+        for (int i = 0; i < nd; ++i) {
+          const int d = lane + 32 * i;
+          if (d < D) dot += qv[i] * Elem<T>::to_f(kg[off + d]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        const float sc = dot * p.scale;
+        const float mn = fmaxf(m, sc);
+        const float alpha = expf(m - mn);
+        const float pr = expf(sc - mn);
+        l = l * alpha + pr;
+        for (int i = 0; i < nd; ++i) {
+          const int d = lane + 32 * i;
+          const float vv = (d < D) ? Elem<T>::to_f(vg[off + d]) : 0.f;
+          acc[i] = acc[i] * alpha + pr * vv;
+        }
+        m = mn;
+      }
+    }
+    if (cur_b >= 0) finish(cur_b, e);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// LSE merge of partials: rows of `parts` at stride part_stride (elements of
+// one part); out row r = sum_i exp(lse_i - M) o_i / sum_i exp(lse_i - M).
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ void lse_merge_row(const float* part_o, const float* part_lse, int64_t part_stride_o,
+                              int64_t part_stride_lse, int nparts, int D, T* out_row,
+                              float* lse_out, int tid, int nthr) {
+  float M = -INFINITY;
+  for (int i = 0; i < nparts; ++i) M = fmaxf(M, part_lse[i * part_stride_lse]);
+  if (M == -INFINITY) {
+    for (int d = tid; d < D; d += nthr) out_row[d] = Elem<T>::from_f(__int_as_float(0x7fc00000));
+    if (lse_out != nullptr && tid == 0) *lse_out = -INFINITY;
+    return;
+  }
+  float W = 0.f;
+  for (int i = 0; i < nparts; ++i) W += expf(part_lse[i * part_stride_lse] - M);
+  const float invW = 1.f / W;
+  for (int d = tid; d < D; d += nthr) {
+    float a = 0.f;
+    for (int i = 0; i < nparts; ++i) {
+      const float w = expf(part_lse[i * part_stride_lse] - M);
+      if (w > 0.f) a += w * part_o[i * part_stride_o + d];
+    }
+    out_row[d] = Elem<T>::from_f(a * invW);
+  }
+  if (lse_out != nullptr && tid == 0) *lse_out = M + logf(W);
+}
+
+// One CTA per request: merges the partial slots of split requests, writes NaN
+// rows for requests without pages.  Requests owned by one CTA were finished by
+// the decode kernel and are skipped.
+template <typename T>
+__global__ void page16_decode_combine_kernel(DecodeParams p, int G) {
+  const int b = blockIdx.x;
+  const int64_t T_ = p.g_prefix[p.B];
+  const int64_t first = p.g_prefix[b], last = p.g_prefix[b + 1];
+  const int D = p.D;
+  T* ob = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(b) * p.Hq * D;
+  if (last == first) {
+    for (int i = threadIdx.x; i < p.Hq * D; i += blockDim.x)
+      ob[i] = Elem<T>::from_f(__int_as_float(0x7fc00000));
+    if (p.lse_out != nullptr)
+      for (int i = threadIdx.x; i < p.Hq; i += blockDim.x)
+        p.lse_out[static_cast<int64_t>(b) * p.Hq + i] = -INFINITY;
+    return;
+  }
+  const int c_lo = owner_of_page(first, T_, G), c_hi = owner_of_page(last - 1, T_, G);
+  if (c_lo == c_hi) return;
+  // CTAs between c_lo and c_hi whose page range is empty (possible when T < G)
+  // wrote nothing: their slots are skipped.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int hq = warp; hq < p.Hq; hq += nw) {
+    float M = -INFINITY;
+    for (int c = c_lo; c <= c_hi; ++c) {
+      if (range_start(c, T_, G) == range_start(c + 1, T_, G)) continue;
+      M = fmaxf(M, p.part_lse[(static_cast<int64_t>(c) + b) * p.Hq + hq]);
+    }
+    float W = 0.f;
+    for (int c = c_lo; c <= c_hi; ++c) {
+      if (range_start(c, T_, G) == range_start(c + 1, T_, G)) continue;
+      W += expf(p.part_lse[(static_cast<int64_t>(c) + b) * p.Hq + hq] - M);
+    }
+    const float invW = 1.f / W;
+    for (int d = lane; d < D; d += 32) {
+      float a = 0.f;
+      for (int c = c_lo; c <= c_hi; ++c) {
+        if (range_start(c, T_, G) == range_start(c + 1, T_, G)) continue;
+        const int64_t slot = static_cast<int64_t>(c) + b;
+        a += expf(p.part_lse[slot * p.Hq + hq] - M) * p.part_o[(slot * p.Hq + hq) * D + d];
+      }
+      ob[static_cast<int64_t>(hq) * D + d] = Elem<T>::from_f(a * invW);
+    }
+    if (p.lse_out != nullptr && lane == 0) p.lse_out[static_cast<int64_t>(b) * p.Hq + hq] = M + logf(W);
+  }
+}
+
+template <typename T>
+__global__ void lse_combine_kernel(const float* part_o, const float* part_lse, void* out,
+                                   float* lse_out, int nparts, int rows, int D) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int r = blockIdx.x * nw + warp;
+  if (r >= rows) return;
+  lse_merge_row<T>(part_o + static_cast<int64_t>(r) * D, part_lse + r, static_cast<int64_t>(rows) * D,
+                   rows, nparts, D, reinterpret_cast<T*>(out) + static_cast<int64_t>(r) * D,
+                   lse_out ? lse_out + r : nullptr, lane, 32);
+}
+
+// ---------------------------------------------------------------------------
+// Decode-token append.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void decode_append_kernel(const T* k_new, const T* v_new, T* k_cache, T* v_cache,
+                                     const int32_t* bt, const int32_t* old_lens, int Hkv, int D,
+                                     int max_blocks, int64_t new_sb, int64_t page_stride,
+                                     int64_t bt_sb) {
+  const int b = blockIdx.x;
+  const int old = old_lens[b];
+  if (old < 0 || old >= max_blocks * kPage) return;
+  const int page = bt[static_cast<int64_t>(b) * bt_sb + old / kPage];
+  const int slot = old % kPage;
+  const int64_t dst = static_cast<int64_t>(page) * page_stride + static_cast<int64_t>(slot) * Hkv * D;
+  const int64_t src = static_cast<int64_t>(b) * new_sb;
+  const int n = Hkv * D;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    k_cache[dst + i] = k_new[src + i];
+    v_cache[dst + i] = v_new[src + i];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct WsLayout {
+  size_t prefix_off, lse_off, o_off, total;
+};
+
+WsLayout ws_layout(int batch, int Hq, int D) {
+  const int64_t slots = 2LL * sm_count() + batch;
+  WsLayout w;
+  w.prefix_off = 0;
+  w.lse_off = align_up(sizeof(int32_t) * (static_cast<size_t>(batch) + 1), 256);
+  w.o_off = w.lse_off + align_up(sizeof(float) * slots * Hq, 256);
+  w.total = w.o_off + align_up(sizeof(float) * slots * Hq * D, 256);
+  return w;
+}
+
+// Raises the dynamic shared memory limit of `kernel` once per device; `done`
+// is the caller's per-kernel flag array.
+template <typename K>
+bool set_smem(K kernel, size_t bytes, bool* done) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && done[dev]) return true;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(bytes)) != cudaSuccess)
+    return false;
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return true;
+}
+
+template <typename T, int D, int NW, int NS>
+int launch_mma(DecodeParams& p, cudaStream_t st) {
+  const int groups = (p.Hkv + NW - 1) / NW;
+  const int G = max(1, sm_count() / groups);
+  const size_t smem = static_cast<size_t>(NW) * NS * 2 * 16 * D * 2 + sizeof(int) * (p.B + 1);
+  auto kern = page16_decode_mma_kernel<T, D, NW, NS>;
+  static bool done[64] = {false};
+  if (!set_smem(kern, NW * NS * 2 * 16 * D * 2 + sizeof(int) * 4097, done)) {
+    set_error("page16_native_launch:smem_attr");
+    return BPKV_ERR_CUDA;
+  }
+  kern<<<dim3(G, groups), NW * 32, smem, st>>>(p);
+  page16_decode_combine_kernel<T><<<p.B, 256, 0, st>>>(p, G);
+  BPKV_RETURN_LAUNCH("page16_native_launch");
+}
+
+template <typename T>
+int launch_generic(DecodeParams& p, cudaStream_t st) {
+  constexpr int NW = 8;
+  const int G = sm_count();
+  const size_t smem = sizeof(int) * (p.B + 1);
+  auto kern = page16_decode_generic_kernel<T, NW>;
+  static bool done[64] = {false};
+  if (smem > 48 * 1024 && !set_smem(kern, sizeof(int) * (16384 + 1), done)) {
+    set_error("page16_native_launch:smem_attr");
+    return BPKV_ERR_CUDA;
+  }
+  kern<<<G, NW * 32, smem, st>>>(p);
+  page16_decode_combine_kernel<T><<<p.B, 256, 0, st>>>(p, G);
+  BPKV_RETURN_LAUNCH("page16_native_launch");
+}
+
+template <typename T>
+int dispatch(DecodeParams& p, cudaStream_t st, bool fast_ok) {
+  if constexpr (!std::is_same<T, float>::value) {
+    if (fast_ok) {
+    if (p.D == 128) return launch_mma<T, 128, 8, 3>(p, st);
+    if (p.D == 64) return launch_mma<T, 64, 8, 6>(p, st);
+    if (p.D == 256) return launch_mma<T, 256, 4, 3>(p, st);
+    }
+  }
+  return launch_generic<T>(p, st);
+}
+
+}  // namespace
+}  // namespace bpkv
+
+using namespace bpkv;
+
+extern "C" BPKV_API size_t bpkv_page16_decode_workspace_size(int batch, int num_q_heads, int num_kv_heads,
+                                                    int head_dim, int dtype) {
+  (void)num_kv_heads;
+  (void)dtype;
+  if (batch <= 0 || num_q_heads <= 0 || head_dim <= 0) return 0;
+  return ws_layout(batch, num_q_heads, head_dim).total;
+}
+
+extern "C" BPKV_API int bpkv_page16_decode(const void* q, const void* k_cache, const void* v_cache,
+                                  const int32_t* block_table, const int32_t* cache_seqlens,
+                                  void* out, float* lse_out, int batch, int num_q_heads,
+                                  int num_kv_heads, int head_dim, int max_blocks,
+                                  int64_t q_stride_b, int64_t q_stride_h, int64_t page_stride,
+                                  int64_t bt_stride_b, float softmax_scale, int dtype,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  clear_error();
+  BPKV_CHECK_ARG(batch > 0 && num_q_heads > 0 && head_dim > 0, "page16_native_shape_unsupported:empty");
+  BPKV_CHECK_ARG(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "page16_native_shape_unsupported:gqa");
+  BPKV_CHECK_ARG(head_dim <= 256, "page16_native_shape_unsupported:head_dim_%d", head_dim);
+  BPKV_CHECK_ARG(max_blocks >= 0, "page16_native_shape_unsupported:block_table_rank");
+  BPKV_CHECK_ARG(batch <= 16384, "page16_native_shape_unsupported:batch_%d", batch);
+  BPKV_CHECK_ARG(dtype == BPKV_F32 || dtype == BPKV_F16 || dtype == BPKV_BF16,
+                 "page16_native_shape_unsupported:dtype_%d", dtype);
+  BPKV_CHECK_ARG(q && k_cache && v_cache && cache_seqlens && out, "page16_native_shape_unsupported:null_pointer");
+  BPKV_CHECK_ARG(max_blocks == 0 || block_table != nullptr, "page16_native_shape_unsupported:null_pointer");
+  const WsLayout w = ws_layout(batch, num_q_heads, head_dim);
+  if (workspace == nullptr || workspace_bytes < w.total) {
+    set_error("page16_native_workspace:need_%zu_bytes", w.total);
+    return BPKV_ERR_WORKSPACE;
+  }
+  DecodeParams p;
+  p.q = q;
+  p.k = k_cache;
+  p.v = v_cache;
+  p.bt = block_table;
+  p.lens = cache_seqlens;
+  p.out = out;
+  p.lse_out = lse_out;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.g_prefix = reinterpret_cast<int32_t*>(ws + w.prefix_off);
+  p.part_lse = reinterpret_cast<float*>(ws + w.lse_off);
+  p.part_o = reinterpret_cast<float*>(ws + w.o_off);
+  p.B = batch;
+  p.Hq = num_q_heads;
+  p.Hkv = num_kv_heads;
+  p.D = head_dim;
+  p.max_blocks = max_blocks;
+  p.n_rep = num_q_heads / num_kv_heads;
+  p.q_sb = q_stride_b;
+  p.q_sh = q_stride_h;
+  p.page_stride = page_stride;
+  p.bt_sb = bt_stride_b;
+  p.scale = softmax_scale;
+  p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  const bool fast_ok = dtype != BPKV_F32 && (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
+                       p.n_rep <= 16 && batch <= 4096 && aligned16(q) && aligned16(k_cache) &&
+                       aligned16(v_cache) && aligned16(out) && (q_stride_b % 8 == 0) &&
+                       (q_stride_h % 8 == 0) && (page_stride % 8 == 0);
+  if (dtype == BPKV_BF16) return dispatch<__nv_bfloat16>(p, st, fast_ok);
+  if (dtype == BPKV_F16) return dispatch<__half>(p, st, fast_ok);
+  return dispatch<float>(p, st, false);
+}
+
+extern "C" BPKV_API int bpkv_lse_combine(const float* part_out, const float* part_lse, void* out,
+                                float* lse_out, int num_parts, int rows, int head_dim,
+                                int out_dtype, void* stream) {
+  clear_error();
+  BPKV_CHECK_ARG(num_parts > 0 && rows >= 0 && head_dim > 0, "lse_combine_shape_unsupported:empty");
+  BPKV_CHECK_ARG(part_out && part_lse && out, "lse_combine_shape_unsupported:null_pointer");
+  if (rows == 0) return BPKV_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nw = 8;
+  const int grid = (rows + nw - 1) / nw;
+  if (out_dtype == BPKV_F32)
+    lse_combine_kernel<float><<<grid, nw * 32, 0, st>>>(part_out, part_lse, out, lse_out, num_parts, rows, head_dim);
+  else if (out_dtype == BPKV_F16)
+    lse_combine_kernel<__half><<<grid, nw * 32, 0, st>>>(part_out, part_lse, out, lse_out, num_parts, rows, head_dim);
+  else if (out_dtype == BPKV_BF16)
+    lse_combine_kernel<__nv_bfloat16><<<grid, nw * 32, 0, st>>>(part_out, part_lse, out, lse_out, num_parts, rows, head_dim);
+  else
+    BPKV_CHECK_ARG(false, "lse_combine_shape_unsupported:dtype_%d", out_dtype);
+  BPKV_RETURN_LAUNCH("lse_combine_launch");
+}
+
+extern "C" BPKV_API int bpkv_decode_append(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                                  const int32_t* block_table, const int32_t* old_lens, int batch,
+                                  int num_kv_heads, int head_dim, int max_blocks,
+                                  int64_t new_stride_b, int64_t page_stride, int64_t bt_stride_b,
+                                  int dtype, void* stream) {
+  clear_error();
+  BPKV_CHECK_ARG(batch >= 0 && num_kv_heads > 0 && head_dim > 0 && max_blocks >= 0,
+                 "decode_append_shape_unsupported:empty");
+  if (batch == 0 || max_blocks == 0) return BPKV_OK;
+  BPKV_CHECK_ARG(k_new && v_new && k_cache && v_cache && block_table && old_lens,
+                 "decode_append_shape_unsupported:null_pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int thr = 256;
+#define BPKV_APPEND(TY)                                                                     \
+  decode_append_kernel<TY><<<batch, thr, 0, st>>>(                                          \
+      static_cast<const TY*>(k_new), static_cast<const TY*>(v_new), static_cast<TY*>(k_cache), \
+      static_cast<TY*>(v_cache), block_table, old_lens, num_kv_heads, head_dim, max_blocks,   \
+      new_stride_b, page_stride, bt_stride_b)
+  if (dtype == BPKV_F32) BPKV_APPEND(float);
+  else if (dtype == BPKV_F16) BPKV_APPEND(__half);
+  else if (dtype == BPKV_BF16) BPKV_APPEND(__nv_bfloat16);
+  else BPKV_CHECK_ARG(false, "decode_append_shape_unsupported:dtype_%d", dtype);
+#undef BPKV_APPEND
+  BPKV_RETURN_LAUNCH("decode_append_launch");
+}

@@ -45,16 +45,16 @@ def page16_decode_reference(q, k_cache, v_cache, block_table, cache_seqlens, sof
             out[b] = np.nan
             lse[b] = -np.inf
             continue
-        k = k.astype(compute_dtype)
-        v = v.astype(compute_dtype)
-        # repeat_kv: q-head h reads kv-head h // n_rep
-        kr = np.repeat(k, n_rep, axis=0)  # [h_q, T, d]
-        vr = np.repeat(v, n_rep, axis=0)
-        s = np.einsum("hd,htd->ht", q[b].astype(compute_dtype), kr) * compute_dtype(softmax_scale)
+        k = k.astype(compute_dtype, copy=False)
+        v = v.astype(compute_dtype, copy=False)
+        qb = q[b].astype(compute_dtype).reshape(k.shape[0], n_rep, -1)
+        # repeat_kv semantics (q-head h reads kv-head h // n_rep), one BLAS matmul per kv head
+        s = np.matmul(qb, k.transpose(0, 2, 1)).reshape(k.shape[0] * n_rep, -1) * compute_dtype(softmax_scale)
         m = s.max(axis=1, keepdims=True)
         p = np.exp(s - m)
         l = p.sum(axis=1, keepdims=True)
-        out[b] = np.einsum("ht,htd->hd", p, vr) / l
+        pv = np.matmul(p.reshape(k.shape[0], n_rep, -1), v).reshape(k.shape[0] * n_rep, -1)
+        out[b] = pv / l
         lse[b] = (m + np.log(l))[:, 0]
     return (out, lse) if return_lse else out
 

@@ -1,0 +1,98 @@
+"""GPU parity of the paged chunked-prefill and varlen prefill kernels against
+the causal-attention oracle (fp64 on the same rounded inputs), max-abs 2e-3
+after rounding the oracle to the output dtype."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.prefill import chunk_attention
+
+pytestmark = pytest.mark.gpu
+
+
+def _err(out, ref, dtype):
+    """Max-abs error beyond the output format's own rounding.
+
+    The output has q's dtype (as in the reference, empty_like(q)); storing a value
+    x in bf16 / fp16 alone costs up to |x| * 2^-8 / 2^-11, so the 2e-3 budget
+    bounds the arithmetic error on top of that unavoidable rounding.
+    """
+    ref = np.asarray(ref, np.float64)
+    fmt = {torch.bfloat16: 2.0 ** -8, torch.float16: 2.0 ** -11}.get(dtype, 0.0)
+    return float(np.nanmax(np.abs(out - ref) - fmt * np.abs(ref)))
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hq,hkv,d", [(32, 8, 128), (8, 8, 64), (16, 2, 128), (4, 1, 256)])
+def test_varlen_prefill(cuda, dtype, hq, hkv, d):
+    from unifiedkv_b200.varlen import varlen_prefill_attention
+    lens = [1, 17, 64, 100, 300]
+    total = sum(lens)
+    g = torch.Generator(device=cuda).manual_seed(hq + d)
+    Q = torch.randn(total, hq, d, generator=g, device=cuda).to(dtype)
+    K = torch.randn(total, hkv, d, generator=g, device=cuda).to(dtype)
+    V = torch.randn(total, hkv, d, generator=g, device=cuda).to(dtype)
+    out = varlen_prefill_attention(Q, K, V, lens).float().cpu().numpy()
+    Qn, Kn, Vn = (t.float().cpu().numpy() for t in (Q, K, V))
+    off = 0
+    for n in lens:
+        ref = chunk_attention(Qn[off:off + n], Kn[off:off + n], Vn[off:off + n])
+        assert _err(out[off:off + n], ref, dtype) < 2e-3
+        off += n
+
+
+def test_varlen_matches_flash_attn_if_present(cuda):
+    fa = pytest.importorskip("flash_attn")
+    from unifiedkv_b200.varlen import build_cu_seqlens, varlen_prefill_attention
+    lens = [5, 128, 333]
+    Q = torch.randn(sum(lens), 32, 128, device=cuda, dtype=torch.bfloat16)
+    K = torch.randn(sum(lens), 8, 128, device=cuda, dtype=torch.bfloat16)
+    V = torch.randn_like(K)
+    ours = varlen_prefill_attention(Q, K, V, lens)
+    cu = build_cu_seqlens(lens, cuda)
+    theirs = fa.flash_attn_varlen_func(Q, K, V, cu, cu, max(lens), max(lens), causal=True)
+    # flash-attn rounds P to bf16 (up to 2^-9 relative per weight); this build splits P
+    assert (ours.float() - theirs.float()).abs().max().item() < 3e-2
+
+
+@pytest.mark.parametrize("past,chunk", [([0, 16, 100, 4000], [512, 512, 512, 37]), ([7, 0], [1, 300])])
+def test_paged_chunk_prefill(cuda, past, chunk):
+    from unifiedkv_b200.chunked_prefill import append_chunk_kv, paged_chunk_prefill
+    hq, hkv, d, dtype = 32, 8, 128, torch.bfloat16
+    rng = np.random.default_rng(sum(past))
+    B = len(past)
+    totals = [p + c for p, c in zip(past, chunk)]
+    need = [math.ceil(t / 16) for t in totals]
+    n_pages = sum(need) + 10
+    perm = rng.permutation(n_pages)
+    g = torch.Generator(device=cuda).manual_seed(1)
+    kc = torch.randn(n_pages, 16, hkv, d, generator=g, device=cuda).to(dtype)
+    vc = torch.randn(n_pages, 16, hkv, d, generator=g, device=cuda).to(dtype)
+    bt = np.zeros((B, max(need)), np.int32)
+    off = 0
+    ids = []
+    for b in range(B):
+        bt[b, :need[b]] = perm[off:off + need[b]]
+        ids.append([int(x) for x in bt[b, :need[b]]])
+        off += need[b]
+    # write each chunk's K/V through the append path, then attend
+    k_new = [torch.randn(hkv, c, d, generator=g, device=cuda).to(dtype) for c in chunk]
+    v_new = [torch.randn(hkv, c, d, generator=g, device=cuda).to(dtype) for c in chunk]
+    for b in range(B):
+        append_chunk_kv(kc, vc, k_new[b], v_new[b], ids[b], past[b])
+    q = torch.randn(sum(chunk), hq, d, generator=g, device=cuda).to(dtype)
+    out = paged_chunk_prefill(q, kc, vc, torch.from_numpy(bt).to(cuda), past, chunk, d ** -0.5, hq // hkv)
+    out = out.float().cpu().numpy()
+    qn = q.float().cpu().numpy()
+    qo = 0
+    for b in range(B):
+        pages = torch.tensor(ids[b], device=cuda, dtype=torch.long)
+        kb = kc.index_select(0, pages).reshape(-1, hkv, d)[:totals[b]].float().cpu().numpy()
+        vb = vc.index_select(0, pages).reshape(-1, hkv, d)[:totals[b]].float().cpu().numpy()
+        # the appended chunk really is in the pool
+        assert np.array_equal(kb[past[b]:], k_new[b].transpose(0, 1).float().cpu().numpy())
+        ref = chunk_attention(qn[qo:qo + chunk[b]], kb, vb)
+        assert _err(out[qo:qo + chunk[b]], ref, dtype) < 2e-3
+        qo += chunk[b]

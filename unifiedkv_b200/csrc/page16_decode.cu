@@ -327,11 +327,11 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
       acc[n][2] *= a1;
       acc[n][3] *= a1;
     }
-    uint32_t pa[4];
-    pa[0] = pack2<T>(pr[0], pr[1]);
-    pa[1] = pack2<T>(pr[2], pr[3]);
-    pa[2] = pack2<T>(pr[4], pr[5]);
-    pa[3] = pack2<T>(pr[6], pr[7]);
+    uint32_t pa[4], pl[4];
+    split2<T>(pr[0], pr[1], pa[0], pl[0]);
+    split2<T>(pr[2], pr[3], pa[1], pl[1]);
+    split2<T>(pr[4], pr[5], pa[2], pl[2]);
+    split2<T>(pr[6], pr[7], pa[3], pl[3]);
     // ---- O += P V ----
     {
       const int mi = lane >> 3, rr = lane & 7;
@@ -343,6 +343,10 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
         ldmatrix_x4_trans(sv + tok * ROWB + ((ch ^ rr) << 4), b0r, b1r, b2r, b3r);
         mma16816<T>(acc[2 * dt], pa, b0r, b1r);
         mma16816<T>(acc[2 * dt + 1], pa, b2r, b3r);
+        if constexpr (SplitP<T>::value) {
+          mma16816<T>(acc[2 * dt], pl, b0r, b1r);
+          mma16816<T>(acc[2 * dt + 1], pl, b2r, b3r);
+        }
       }
     }
     __syncwarp();

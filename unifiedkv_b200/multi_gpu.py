@@ -1,0 +1,156 @@
+"""Multi-GPU decode: request sharding and split-KV for one long sequence.
+
+Replaces ``MultiGPUCoordinator`` (core/multi_gpu.py:7-123), which runs in one
+process, shards KV *heads* across GPUs, mirrors every prefill layer and decode
+token to each GPU with ``.to('cuda:i')`` copies, and never uses a collective
+(multi-GPU decode falls back to dense rebuild, core/engine.py:2841-2851).
+
+B200 design: one process per GPU (``torch.distributed``, NCCL over NVLink).
+  * Requests are independent: ``shard_requests`` assigns whole requests to
+    ranks, balanced by page count; each rank owns a pool and decodes its own
+    requests.  No collective on the data path.
+  * One very long sequence: ``split_pages`` gives each rank a contiguous range
+    of the sequence's pages; each rank runs Page16 decode on its range with
+    ``lse_out`` and the ranks exchange [rows, d] fp32 partials plus [rows] lse
+    with one NCCL all-gather, merged by the log-sum-exp combine kernel.
+The constructor arguments and the watermark / release methods of the
+reference coordinator are kept; KV-head sharding is not (Page16 needs all
+heads of a page on one GPU).
+"""
+from __future__ import annotations
+
+import heapq
+from typing import Callable, Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from .pool import PagedKVPool
+
+
+def shard_requests(lengths: Sequence[int], world: int) -> List[int]:
+    """Owner rank of every request: longest-processing-time-first over page
+    counts (deterministic: ties by request index, then lowest rank)."""
+    pages = [(-((int(l) + 15) // 16), i) for i, l in enumerate(lengths)]
+    pages.sort()
+    heap = [(0, r) for r in range(world)]
+    owner = [0] * len(lengths)
+    for neg_p, i in pages:
+        load, r = heapq.heappop(heap)
+        owner[i] = r
+        heapq.heappush(heap, (load - neg_p, r))
+    return owner
+
+
+def split_pages(n_pages: int, world: int) -> List[Tuple[int, int]]:
+    """Contiguous [start, end) page ranges per rank, sizes differing by <= 1."""
+    return [(r * n_pages // world, (r + 1) * n_pages // world) for r in range(world)]
+
+
+def local_range_lens(total_len: int, start_page: int, end_page: int) -> int:
+    """Tokens of a sequence of total_len that fall in pages [start, end)."""
+    return max(0, min(total_len, 16 * end_page) - 16 * start_page)
+
+
+def exchange_partials(out_part: torch.Tensor, lse_part: torch.Tensor, group=None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """All-gather per-rank partials: out_part fp32 [rows, d], lse fp32 [rows]
+    -> ([world, rows, d], [world, rows]).  One collective: both travel packed
+    in a single [rows, d+1] fp32 buffer."""
+    world = dist.get_world_size(group)
+    rows, d = out_part.shape
+    packed = torch.cat([out_part.reshape(rows, d).float(), lse_part.reshape(rows, 1).float()], dim=1).contiguous()
+    flat = torch.empty((world * rows, d + 1), dtype=torch.float32, device=packed.device)
+    dist.all_gather_into_tensor(flat, packed, group=group)
+    gathered = flat.view(world, rows, d + 1)
+    return gathered[..., :d].contiguous(), gathered[..., d].contiguous()
+
+
+def _native_merge(parts: torch.Tensor, lses: torch.Tensor, out_dtype: torch.dtype):
+    from .page16_native import lse_combine
+    return lse_combine(parts, lses, out_dtype, return_lse=True)
+
+
+def split_kv_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, local_block_table: torch.Tensor,
+                    local_lens: torch.Tensor, softmax_scale: float, n_rep: int, group=None,
+                    merge: Optional[Callable] = None) -> torch.Tensor:
+    """Decode one (or a few) sequences whose pages are split across ranks.
+
+    Each rank passes q (identical on all ranks, [B, h_q, d]), its own pool
+    view, the block table of ITS page range and the token count in that range.
+    Returns the merged [B, h_q, d] output on every rank.  A rank whose range
+    is empty contributes lse = -inf (nothing).
+    """
+    from .page16_native import page16_decode_attention
+    B, hq, d = [int(x) for x in q.shape]
+    lse = torch.empty((B, hq), dtype=torch.float32, device=q.device)
+    part = page16_decode_attention(q, k_cache, v_cache, local_block_table, local_lens, softmax_scale=softmax_scale,
+                                   n_rep=n_rep, lse_out=lse)
+    parts, lses = exchange_partials(part.float().reshape(B * hq, d), lse.reshape(B * hq), group)
+    merge = merge or _native_merge
+    out, _ = merge(parts, lses, q.dtype)
+    return out.reshape(B, hq, d)
+
+
+class MultiGPUCoordinator:
+    """Per-rank coordinator (one process per GPU).
+
+    Keeps the reference constructor signature (core/multi_gpu.py:8-47); the
+    pool of this rank holds ALL KV heads (``num_kv_heads_total``) and the
+    requests this rank owns.
+    """
+
+    def __init__(self, num_gpus: int, block_size: int, num_layers: int, num_kv_heads_total: int, head_dim: int,
+                 dtype: torch.dtype = torch.float16, cpu_mem_gb_per_gpu: float = 16.0, *, group=None,
+                 n_pages: Optional[int] = None, device: Optional[torch.device] = None):
+        self.group = group
+        self.distributed = dist.is_available() and dist.is_initialized()
+        self.world = dist.get_world_size(group) if self.distributed else 1
+        self.rank = dist.get_rank(group) if self.distributed else 0
+        if int(num_gpus) != self.world:
+            raise RuntimeError(f"multi_gpu_world_mismatch num_gpus={num_gpus} world={self.world}")
+        self.num_gpus = int(num_gpus)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.pool = PagedKVPool(block_size, num_layers, num_kv_heads_total, head_dim, dtype,
+                                gpu_mem_frac=0.9, cpu_mem_gb=cpu_mem_gb_per_gpu, device=self.device, n_total=n_pages)
+        self.owner: Dict[int, int] = {}
+        self.local_blocks: Dict[int, List[int]] = {}
+
+    def assign(self, seq_lens: Dict[int, int]) -> Dict[int, int]:
+        """Shard new requests {seq_id: length} over ranks; returns {seq_id: rank}."""
+        ids = sorted(seq_lens)
+        owners = shard_requests([seq_lens[i] for i in ids], self.world)
+        for sid, r in zip(ids, owners):
+            self.owner[sid] = r
+        return {sid: self.owner[sid] for sid in ids}
+
+    def is_local(self, seq_id: int) -> bool:
+        return self.owner.get(int(seq_id), 0) == self.rank
+
+    def allocate(self, seq_id: int, n_blocks: int) -> List[int]:
+        if not self.is_local(seq_id):
+            raise RuntimeError(f"multi_gpu_not_owner seq={seq_id} rank={self.rank}")
+        ids = self.pool.allocate_blocks(n_blocks)
+        if not ids:
+            raise MemoryError(f"Cannot allocate {n_blocks} blocks for seq={seq_id} on rank {self.rank}")
+        self.local_blocks.setdefault(int(seq_id), []).extend(ids)
+        return ids
+
+    def global_watermark(self) -> str:
+        """Worst free ratio over ranks (core/multi_gpu.py:112-119 thresholds)."""
+        ratio = self.pool.n_free / max(1, self.pool.N_total)
+        if self.distributed and self.world > 1:
+            dev = self.device if dist.get_backend(self.group) == "nccl" else torch.device("cpu")
+            t = torch.tensor([ratio], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=self.group)
+            ratio = float(t.item())
+        if ratio < 0.15:
+            return "VRAM_FULL"
+        if ratio < 0.35:
+            return "WARNING"
+        return "OK"
+
+    def release_all(self, seq_id: int) -> None:
+        ids = self.local_blocks.pop(int(seq_id), None)
+        if ids:
+            self.pool.free_blocks_by_ids(ids)
+        self.owner.pop(int(seq_id), None)

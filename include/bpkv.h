@@ -87,6 +87,32 @@ BPKV_API int bpkv_page16_decode(const void* q, const void* k_cache, const void* 
                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ *
+ * Allocation-free Page16 decode.  No counterpart in the reference: this entry
+ * point exists for callers of this library that cannot allocate device memory
+ * when they decode - an engine that reserved nearly all of HBM for the paged
+ * pool up front, a non-Python host binding this C ABI without a device
+ * allocator, or a latency-critical loop that must avoid cudaMalloc's implicit
+ * synchronisation.  Same arguments and results as bpkv_page16_decode minus
+ * the workspace: the scratch is a file-scope device array of
+ * bpkv_page16_decode_noalloc_max_scratch() bytes (16 MiB), held by every GPU
+ * that loads the library until exit.  Shapes whose scratch
+ * (bpkv_page16_decode_workspace_size) exceeds it are rejected with
+ * BPKV_ERR_WORKSPACE.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) and should come before any stream capture.
+ * All calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  It calls no cudaMalloc / cudaFree.
+ * ------------------------------------------------------------------------ */
+BPKV_API size_t bpkv_page16_decode_noalloc_max_scratch(void);
+
+BPKV_API int bpkv_page16_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                       const int32_t* block_table, const int32_t* cache_seqlens,
+                       void* out, float* lse_out,
+                       int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                       int max_blocks, int64_t q_stride_b, int64_t q_stride_h,
+                       int64_t page_stride, int64_t bt_stride_b,
+                       float softmax_scale, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------ *
  * Log-sum-exp merge of partial attention results (split-KV across GPUs).
  * The reference has no counterpart: it never splits a sequence across GPUs
  * (core/multi_gpu.py:7-123 only mirrors KV-head shards).  This merge completes

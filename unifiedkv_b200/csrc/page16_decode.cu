@@ -21,6 +21,7 @@
 //    the M rows; P is reused straight from the S accumulators as the A
 //    fragment.  Online softmax in the exp2 domain, row max / sum by quad
 //    shuffles.
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -758,4 +759,80 @@ extern "C" BPKV_API int bpkv_decode_append(const void* k_new, const void* v_new,
   else BPKV_CHECK_ARG(false, "decode_append_shape_unsupported:dtype_%d", dtype);
 #undef BPKV_APPEND
   BPKV_RETURN_LAUNCH("decode_append_launch");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of bpkv_page16_decode.
+//
+// Some callers cannot allocate device memory at decode time: an engine that
+// has handed (nearly) all of HBM to the paged pool up front, a host written in
+// another language that reaches this library through a plain C FFI and owns no
+// device allocator, or a latency-critical loop that must not hit cudaMalloc's
+// implicit device synchronisation.  For them the split-KV scratch (request
+// page prefix, per-slot partial outputs and log-sum-exps) lives in one
+// file-scope device array of fixed size, kNoAllocScratchBytes, which every GPU
+// that loads this library holds until the process exits.
+//
+// The array's host-side name is not a device address, so the address is
+// looked up with cudaGetSymbolAddress once per device (with that device
+// current) on the first call made on that device; make that first call before
+// any stream capture.  Every call shares the same array: calls whose kernels
+// overlap on the GPU (different streams, or different host threads without
+// ordering) race on it and must be serialised by the caller.  Nothing in it
+// has to start at zero: each call writes every scratch byte it later reads.
+// ---------------------------------------------------------------------------
+namespace bpkv {
+namespace {
+constexpr size_t kNoAllocScratchBytes = 16u << 20;  // 16 MiB
+__device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+void* noalloc_scratch_ptr(int* err) {
+  static std::mutex mu;
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = 1;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(mu);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("page16_native_noalloc:cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      *err = 2;
+      return nullptr;
+    }
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+}  // namespace
+}  // namespace bpkv
+
+extern "C" BPKV_API size_t bpkv_page16_decode_noalloc_max_scratch(void) { return bpkv::kNoAllocScratchBytes; }
+
+extern "C" BPKV_API int bpkv_page16_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                                   const int32_t* block_table, const int32_t* cache_seqlens,
+                                                   void* out, float* lse_out, int batch, int num_q_heads,
+                                                   int num_kv_heads, int head_dim, int max_blocks,
+                                                   int64_t q_stride_b, int64_t q_stride_h, int64_t page_stride,
+                                                   int64_t bt_stride_b, float softmax_scale, int dtype,
+                                                   void* stream) {
+  clear_error();
+  BPKV_CHECK_ARG(batch > 0 && num_q_heads > 0 && head_dim > 0, "page16_native_shape_unsupported:empty");
+  const size_t need = ws_layout(batch, num_q_heads, head_dim).total;
+  if (need > kNoAllocScratchBytes) {
+    set_error("page16_native_noalloc:scratch_need_%zu_bytes_exceeds_max_%zu", need, kNoAllocScratchBytes);
+    return BPKV_ERR_WORKSPACE;
+  }
+  int err = 0;
+  void* scratch = noalloc_scratch_ptr(&err);
+  if (scratch == nullptr) {
+    if (err == 1) set_error("page16_native_noalloc:no_current_device");
+    return BPKV_ERR_CUDA;
+  }
+  return bpkv_page16_decode(q, k_cache, v_cache, block_table, cache_seqlens, out, lse_out, batch, num_q_heads,
+                            num_kv_heads, head_dim, max_blocks, q_stride_b, q_stride_h, page_stride, bt_stride_b,
+                            softmax_scale, dtype, scratch, kNoAllocScratchBytes, stream);
 }

@@ -196,13 +196,18 @@ def run_reference(args, rank: int, world: int) -> None:
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
-def setup_rank(rank: int, device, seed_base: int = 2024):
+def setup_rank(rank: int, device, seed_base: int = 2024, small: bool = False):
     import torch
+    global LAYERS
     rng, lens = make_requests(seed_base + rank)
-    total = torch.cuda.get_device_properties(device).total_memory
-    page_bytes = 2 * LAYERS * 16 * HKV * D * 2  # K and V pages of all layers
-    n_pages = int(POOL_FRAC * total) // page_bytes
     need = (lens + 15) // 16
+    if small:  # profiling case: one layer, pool of just the needed pages (~2.5 GB)
+        LAYERS = 1
+        n_pages = int(need.sum()) + 64
+    else:
+        total = torch.cuda.get_device_properties(device).total_memory
+        page_bytes = 2 * LAYERS * 16 * HKV * D * 2  # K and V pages of all layers
+        n_pages = int(POOL_FRAC * total) // page_bytes
     assert int(need.sum()) <= n_pages
     k_pool = torch.empty((LAYERS, n_pages, 16, HKV, D), dtype=torch.bfloat16, device=device)
     v_pool = torch.empty_like(k_pool)
@@ -227,7 +232,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    st = setup_rank(rank, device)
+    st = setup_rank(rank, device, small=args.profile_small)
     k_pool, v_pool, qs = st["k_pool"], st["v_pool"], st["qs"]
     bt_d = torch.from_numpy(st["bt"]).to(device)
     lens_d = torch.from_numpy(st["lens"]).to(device)
@@ -342,7 +347,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         "gpu_launches": 2 * LAYERS * args.steps,
         "clocks": clocks.summary(),
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if args.profile_small:
+        line["config"]["workload"] += " [profiling case: 1 layer, compact pool]"
+    if world == 1 and not args.no_cpu_baseline and not args.profile_small:
         line["cpu_baseline"] = cpu_baseline_block(cpu_sample())
     print(json.dumps(line), flush=True)
 
@@ -354,6 +361,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-small", action="store_true",
+                    help="ncu case: 1 layer, pool of only the needed pages (same per-launch work)")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

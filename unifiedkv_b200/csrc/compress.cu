@@ -271,7 +271,7 @@ __device__ __forceinline__ uint32_t desc_key(float f) {
 }
 
 __global__ void __launch_bounds__(1024) topk_select_kernel(const float* scores, int n, int k, int32_t* selected) {
-  extern __shared__ __align__(16) uint8_t smem[];
+  extern __shared__ __align__(128) uint8_t smem[];
   int npow = 1;
   while (npow < n) npow <<= 1;
   uint64_t* key = reinterpret_cast<uint64_t*>(smem);

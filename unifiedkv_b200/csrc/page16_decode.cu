@@ -486,52 +486,74 @@ __device__ void lse_merge_row(const float* part_o, const float* part_lse, int64_
   if (lse_out != nullptr && tid == 0) *lse_out = M + logf(W);
 }
 
-// One CTA per request: merges the partial slots of split requests, writes NaN
-// rows for requests without pages.  Requests owned by one CTA were finished by
-// the decode kernel and are skipped.
+// Combine of split requests.  CTA (b, head group of kCombineHeads) gathers the
+// list of CTAs that own pages of request b (ranges can be empty when T < G;
+// those wrote nothing and are skipped), turns the per-slot lse into normalised
+// weights once in shared memory, then forms out = sum_i w_i o_i with coalesced
+// reads.  Requests without pages get NaN rows (the reference's 0/0); requests
+// owned by a single CTA were finished by the decode kernel and are skipped.
+constexpr int kCombineHeads = 8;
+constexpr int kMaxSlotsPerReq = 1024;  // >= 2 * SM count
+
 template <typename T>
-__global__ void page16_decode_combine_kernel(DecodeParams p, int G) {
+__global__ void __launch_bounds__(256) page16_decode_combine_kernel(DecodeParams p, int G) {
+  __shared__ int s_slot[kMaxSlotsPerReq];
+  __shared__ float s_w[kCombineHeads][kMaxSlotsPerReq];
+  __shared__ float s_lse[kCombineHeads];
+  __shared__ int s_n;
   const int b = blockIdx.x;
+  const int h0 = blockIdx.y * kCombineHeads;
+  const int nh = min(kCombineHeads, p.Hq - h0);
   const int64_t T_ = p.g_prefix[p.B];
   const int64_t first = p.g_prefix[b], last = p.g_prefix[b + 1];
   const int D = p.D;
-  T* ob = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(b) * p.Hq * D;
+  T* ob = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.Hq + h0) * D;
   if (last == first) {
-    for (int i = threadIdx.x; i < p.Hq * D; i += blockDim.x)
-      ob[i] = Elem<T>::from_f(__int_as_float(0x7fc00000));
-    if (p.lse_out != nullptr)
-      for (int i = threadIdx.x; i < p.Hq; i += blockDim.x)
-        p.lse_out[static_cast<int64_t>(b) * p.Hq + i] = -INFINITY;
+    for (int i = threadIdx.x; i < nh * D; i += blockDim.x) ob[i] = Elem<T>::from_f(__int_as_float(0x7fc00000));
+    if (p.lse_out != nullptr && threadIdx.x < nh) p.lse_out[static_cast<int64_t>(b) * p.Hq + h0 + threadIdx.x] = -INFINITY;
     return;
   }
   const int c_lo = owner_of_page(first, T_, G), c_hi = owner_of_page(last - 1, T_, G);
   if (c_lo == c_hi) return;
-  // CTAs between c_lo and c_hi whose page range is empty (possible when T < G)
-  // wrote nothing: their slots are skipped.
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int hq = warp; hq < p.Hq; hq += nw) {
-    float M = -INFINITY;
-    for (int c = c_lo; c <= c_hi; ++c) {
-      if (range_start(c, T_, G) == range_start(c + 1, T_, G)) continue;
-      M = fmaxf(M, p.part_lse[(static_cast<int64_t>(c) + b) * p.Hq + hq]);
+  if (threadIdx.x == 0) {
+    int n = 0;
+    int64_t start = range_start(c_lo, T_, G);
+    for (int c = c_lo; c <= c_hi && n < kMaxSlotsPerReq; ++c) {
+      const int64_t next = range_start(c + 1, T_, G);
+      if (next > start) s_slot[n++] = c + b;
+      start = next;
     }
-    float W = 0.f;
-    for (int c = c_lo; c <= c_hi; ++c) {
-      if (range_start(c, T_, G) == range_start(c + 1, T_, G)) continue;
-      W += expf(p.part_lse[(static_cast<int64_t>(c) + b) * p.Hq + hq] - M);
-    }
-    const float invW = 1.f / W;
-    for (int d = lane; d < D; d += 32) {
-      float a = 0.f;
-      for (int c = c_lo; c <= c_hi; ++c) {
-        if (range_start(c, T_, G) == range_start(c + 1, T_, G)) continue;
-        const int64_t slot = static_cast<int64_t>(c) + b;
-        a += expf(p.part_lse[slot * p.Hq + hq] - M) * p.part_o[(slot * p.Hq + hq) * D + d];
-      }
-      ob[static_cast<int64_t>(hq) * D + d] = Elem<T>::from_f(a * invW);
-    }
-    if (p.lse_out != nullptr && lane == 0) p.lse_out[static_cast<int64_t>(b) * p.Hq + hq] = M + logf(W);
+    s_n = n;
   }
+  __syncthreads();
+  const int n = s_n;
+  // one warp per head: max, sum, normalised weights
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int h = warp; h < nh; h += blockDim.x >> 5) {
+    const int hq = h0 + h;
+    float M = -INFINITY;
+    for (int i = lane; i < n; i += 32) M = fmaxf(M, p.part_lse[static_cast<int64_t>(s_slot[i]) * p.Hq + hq]);
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float W = 0.f;
+    for (int i = lane; i < n; i += 32) {
+      const float w = expf(p.part_lse[static_cast<int64_t>(s_slot[i]) * p.Hq + hq] - M);
+      s_w[h][i] = w;
+      W += w;
+    }
+    for (int o = 16; o > 0; o >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o);
+    const float inv = 1.f / W;
+    for (int i = lane; i < n; i += 32) s_w[h][i] *= inv;
+    if (lane == 0) s_lse[h] = M + logf(W);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < nh * D; e += blockDim.x) {
+    const int h = e / D, d = e % D;
+    const float* po = p.part_o + static_cast<int64_t>(h0 + h) * D + d;
+    float a = 0.f;
+    for (int i = 0; i < n; ++i) a += s_w[h][i] * po[static_cast<int64_t>(s_slot[i]) * p.Hq * D];
+    ob[static_cast<int64_t>(h) * D + d] = Elem<T>::from_f(a);
+  }
+  if (p.lse_out != nullptr && threadIdx.x < nh) p.lse_out[static_cast<int64_t>(b) * p.Hq + h0 + threadIdx.x] = s_lse[threadIdx.x];
 }
 
 template <typename T>
@@ -612,7 +634,7 @@ int launch_mma(DecodeParams& p, cudaStream_t st) {
     return BPKV_ERR_CUDA;
   }
   kern<<<dim3(G, groups), NW * 32, smem, st>>>(p);
-  page16_decode_combine_kernel<T><<<p.B, 256, 0, st>>>(p, G);
+  page16_decode_combine_kernel<T><<<dim3(p.B, (p.Hq + kCombineHeads - 1) / kCombineHeads), 256, 0, st>>>(p, G);
   BPKV_RETURN_LAUNCH("page16_native_launch");
 }
 
@@ -628,7 +650,7 @@ int launch_generic(DecodeParams& p, cudaStream_t st) {
     return BPKV_ERR_CUDA;
   }
   kern<<<G, NW * 32, smem, st>>>(p);
-  page16_decode_combine_kernel<T><<<p.B, 256, 0, st>>>(p, G);
+  page16_decode_combine_kernel<T><<<dim3(p.B, (p.Hq + kCombineHeads - 1) / kCombineHeads), 256, 0, st>>>(p, G);
   BPKV_RETURN_LAUNCH("page16_native_launch");
 }
 

@@ -1,0 +1,376 @@
+"""Pinned-host offload and prefetch of pool pages, batched and asynchronous.
+
+Replaces the transfer mechanism of ``AsyncOffloadManager`` (core/offload.py:547-757):
+there, every (page, layer, K/V) is one small ``copy_`` into a freshly pinned
+host tensor, and ``ensure_sequence_blocks_on_gpu`` synchronises the host
+before decode (core/offload.py:752).  Here:
+  * host memory is one pinned arena of fixed-size slots allocated once; a slot
+    holds one logical page of one sequence for ALL layers, K and V;
+  * an offload gathers the selected pages of every layer into a device
+    staging buffer with one ``bpkv_page_gather`` launch per K/V (the pool is
+    addressed as a flat [L*N] page array), then one device->host copy, all on
+    a low-priority side stream, completed by a CUDA event;
+  * a prefetch is the mirror image (one host->device copy, one
+    ``bpkv_page_scatter`` per K/V); ``ensure_sequence_blocks_on_gpu`` makes the
+    compute stream wait on the prefetch event instead of blocking the host.
+The page-table bookkeeping keeps the reference's names and states
+(``BlockTableEntry.gpu_block_map`` with -1 for host-resident pages,
+``OffloadState``, ``_try_finalize_offload/prefetch``, stats counters).  The
+pressure policy that picks victims (P2) is out of scope.
+"""
+from __future__ import annotations
+
+import threading
+from typing import Dict, List, Optional, Tuple
+
+import torch
+
+from . import _lib
+from .kv_types import BlockTableEntry, DecodeAppendResult, OffloadState
+from .pool import PagedKVPool
+
+
+class AsyncOffloadManager:
+    def __init__(self, pool: PagedKVPool, num_layers: int, host_slots: int = 0, staging_pages: int = 512):
+        self.pool = pool
+        self.num_layers = int(num_layers)
+        self.lock = threading.Lock()
+        self.page_table: Dict[Tuple[int, int], BlockTableEntry] = {}
+        self.device = pool.device
+        self.transfer_stream = torch.cuda.Stream(device=self.device, priority=-1)
+        self.page_elems = 16 * pool.num_kv_heads * pool.head_dim
+        self.staging_pages = int(staging_pages)
+        self.host_slots = int(host_slots) if host_slots else max(1, pool.N_total // 4)
+        self._arena: Optional[torch.Tensor] = None    # pinned [2, slots, L, page_elems]
+        self._staging: Optional[torch.Tensor] = None  # device [2, staging_pages, L, page_elems]
+        self._free_slots: List[int] = list(range(self.host_slots))
+        self._slot_of: Dict[Tuple[int, int], int] = {}  # (seq, logical page) -> host slot
+        self._pending: Dict[int, dict] = {}  # seq -> in-flight transfer
+        self._stats: Dict[str, int] = {}
+
+    # ---- helpers -------------------------------------------------------------
+    def _inc_stat(self, key: str, inc: int = 1):
+        self._stats[key] = self._stats.get(key, 0) + int(inc)
+
+    def get_stats(self, reset: bool = False) -> Dict[str, int]:
+        out = dict(self._stats)
+        if reset:
+            self._stats.clear()
+        return out
+
+    def _ensure_buffers(self):
+        if self._arena is None:
+            self._arena = torch.empty((2, self.host_slots, self.num_layers, self.page_elems), dtype=self.pool.dtype,
+                                      pin_memory=True)
+        if self._staging is None:
+            self._staging = torch.empty((2, self.staging_pages, self.num_layers, self.page_elems),
+                                        dtype=self.pool.dtype, device=self.device)
+
+    @staticmethod
+    def _ensure_entry_maps(entry: BlockTableEntry):
+        n = len(entry.block_ids)
+        if len(entry.gpu_block_map) != n:
+            entry.gpu_block_map = list(entry.block_ids)
+        if len(entry.cpu_k_blocks) != n:
+            entry.cpu_k_blocks = [None] * n
+            entry.cpu_v_blocks = [None] * n
+
+    @staticmethod
+    def _update_entry_state(entry: BlockTableEntry):
+        on_gpu = sum(1 for b in entry.gpu_block_map if int(b) >= 0)
+        if on_gpu == len(entry.gpu_block_map):
+            entry.state = OffloadState.ON_GPU
+        elif on_gpu == 0:
+            entry.state = OffloadState.ON_CPU
+        else:
+            entry.state = OffloadState.MIXED
+
+    def _entries(self, seq_id: int) -> List[BlockTableEntry]:
+        return [self.page_table[(seq_id, l)] for l in range(self.num_layers) if (seq_id, l) in self.page_table]
+
+    def _mark_resident(self, seq_id: int):
+        pass
+
+    def register_sequence(self, seq_id: int, block_ids: List[int], seq_len: int) -> None:
+        """Page-table rows for a sequence whose pages (shared by all layers) are already written."""
+        with self.lock:
+            for l in range(self.num_layers):
+                self.page_table[(int(seq_id), l)] = BlockTableEntry(
+                    seq_id=int(seq_id), layer_id=l, state=OffloadState.ON_GPU, block_ids=list(block_ids),
+                    seq_len=int(seq_len), logical_seq_len=int(seq_len), materialized_blocks=len(block_ids),
+                    gpu_block_map=list(block_ids), cpu_k_blocks=[None] * len(block_ids),
+                    cpu_v_blocks=[None] * len(block_ids))
+
+    def _flat_ids(self, pages: List[int]) -> torch.Tensor:
+        """Flat [L*N] pool page indices, page-major: entry j*L + l is page j of layer l."""
+        N = self.pool.N_total
+        ids = [l * N + p for p in pages for l in range(self.num_layers)]
+        return torch.tensor(ids, dtype=torch.int32).pin_memory().to(self.device, non_blocking=True)
+
+    def _move(self, gather: bool, flat_ids: torch.Tensor, which: int) -> None:
+        """Pool pages <-> staging[which][:n] ([n, L, page_elems]) on the transfer stream."""
+        cache = self.pool.k_cache if which == 0 else self.pool.v_cache
+        stage = self._staging[which]
+        n = int(flat_ids.numel())
+        lib = _lib.lib()
+        code = _lib.dtype_code(self.pool.dtype)
+        st = self.transfer_stream.cuda_stream
+        if gather:
+            rc = lib.bpkv_page_gather(cache.data_ptr(), flat_ids.data_ptr(), n, stage.data_ptr(), self.page_elems,
+                                      self.page_elems, code, st)
+        else:
+            rc = lib.bpkv_page_scatter(stage.data_ptr(), flat_ids.data_ptr(), n, cache.data_ptr(), self.page_elems,
+                                       self.page_elems, code, st)
+        _lib.check(rc, "page_gather" if gather else "page_scatter")
+
+    def _alloc_slots(self, n: int) -> Optional[List[int]]:
+        """n host slots, lowest-first (sorted free list keeps batches mostly contiguous)."""
+        if len(self._free_slots) < n:
+            return None
+        self._free_slots.sort()
+        out, self._free_slots = self._free_slots[:n], self._free_slots[n:]
+        return out
+
+    @staticmethod
+    def _runs(slots: List[int]) -> List[Tuple[int, int, int]]:
+        """(first batch index, first slot, length) of each contiguous slot run."""
+        runs = []
+        i = 0
+        while i < len(slots):
+            j = i
+            while j + 1 < len(slots) and slots[j + 1] == slots[j] + 1:
+                j += 1
+            runs.append((i, slots[i], j - i + 1))
+            i = j + 1
+        return runs
+
+    # ---- offload (device -> pinned host) -----------------------------------
+    def offload_sequence_blocks(self, seq_id: int, logical_block_indices: List[int]) -> bool:
+        """Start copying the given logical pages (all layers, K and V) of a
+        sequence to host slots; pool pages are freed when the copy completes
+        (``_try_finalize_offload``).  Mirrors core/offload.py:547-599."""
+        self._inc_stat('offload_calls')
+        self._try_finalize_offload(seq_id, force_sync=False)
+        self._try_finalize_prefetch(seq_id, force_sync=False)
+        if seq_id in self._pending:
+            self._inc_stat('offload_fail')
+            return False
+        entries = self._entries(seq_id)
+        if not entries or any(e.state not in (OffloadState.ON_GPU, OffloadState.MIXED) for e in entries):
+            self._inc_stat('offload_fail')
+            return False
+        first = entries[0]
+        self._ensure_entry_maps(first)
+        sel = sorted({int(i) for i in logical_block_indices
+                      if 0 <= int(i) < len(first.gpu_block_map) and int(first.gpu_block_map[int(i)]) >= 0})
+        if not sel:
+            self._inc_stat('offload_fail')
+            return False
+        self._ensure_buffers()
+        slots = self._alloc_slots(len(sel))
+        if slots is None:
+            self._inc_stat('offload_fail')
+            return False
+        pages = [int(first.gpu_block_map[i]) for i in sel]
+        ts = self.transfer_stream
+        ts.wait_stream(torch.cuda.current_stream(self.device))  # pages may still be written by compute
+        with torch.cuda.stream(ts):
+            for c0 in range(0, len(sel), self.staging_pages):
+                chunk = pages[c0:c0 + self.staging_pages]
+                ids = self._flat_ids(chunk)
+                for w in (0, 1):
+                    self._move(True, ids, w)
+                    for i, s0, n in self._runs(slots[c0:c0 + len(chunk)]):
+                        self._arena[w, s0:s0 + n].copy_(self._staging[w, i:i + n], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(ts)
+        self._pending[seq_id] = dict(kind="offload", event=ev, sel=sel, pages=pages, slots=slots)
+        for e in entries:
+            e.state = OffloadState.OFFLOAD_INFLIGHT
+            e.transfer_event = ev
+            e.pending_block_indices = list(sel)
+        self._inc_stat('offload_blocks', len(sel))
+        return True
+
+    def offload_sequence(self, seq_id: int) -> bool:
+        entries = self._entries(seq_id)
+        if not entries:
+            self._inc_stat('offload_fail')
+            return False
+        return self.offload_sequence_blocks(seq_id, list(range(len(entries[0].gpu_block_map))))
+
+    def _try_finalize_offload(self, seq_id: int, force_sync: bool = False) -> bool:
+        p = self._pending.get(seq_id)
+        if p is None or p["kind"] != "offload":
+            return False
+        if not force_sync and not p["event"].query():
+            return False
+        p["event"].synchronize()
+        del self._pending[seq_id]
+        for e in self._entries(seq_id):
+            self._ensure_entry_maps(e)
+            for idx, slot in zip(p["sel"], p["slots"]):
+                e.gpu_block_map[idx] = -1
+                e.cpu_k_blocks[idx] = ("host_slot", slot)
+                e.cpu_v_blocks[idx] = ("host_slot", slot)
+            e.transfer_event = None
+            e.pending_block_indices = None
+            self._update_entry_state(e)
+        for idx, slot in zip(p["sel"], p["slots"]):
+            self._slot_of[(seq_id, idx)] = slot
+        self.pool.free_blocks_by_ids(p["pages"])
+        self.pool.cpu_used_bytes += len(p["sel"]) * 2 * self.num_layers * self.page_elems * self.pool.k_cache.element_size()
+        self._inc_stat('offload_success')
+        return True
+
+    # ---- prefetch (pinned host -> device) ------------------------------------
+    def prefetch_sequence_blocks(self, seq_id: int, logical_block_indices: List[int]) -> bool:
+        """Start copying host-resident pages back into fresh pool pages.  Returns
+        True when nothing is left to fetch, False while a transfer is in flight
+        or on failure (core/offload.py:620-691)."""
+        self._inc_stat('prefetch_calls')
+        if self._try_finalize_prefetch(seq_id, force_sync=False):
+            return True
+        if seq_id in self._pending:
+            self._inc_stat('prefetch_inflight')
+            return False
+        entries = self._entries(seq_id)
+        if not entries:
+            self._inc_stat('prefetch_noop')
+            return True
+        first = entries[0]
+        sel = sorted({int(i) for i in logical_block_indices
+                      if 0 <= int(i) < len(first.gpu_block_map) and int(first.gpu_block_map[int(i)]) < 0
+                      and (seq_id, int(i)) in self._slot_of})
+        if not sel:
+            self._inc_stat('prefetch_noop')
+            return True
+        pages = self.pool.allocate_blocks(len(sel))
+        if len(pages) != len(sel):
+            self._inc_stat('prefetch_fail')
+            return False
+        slots = [self._slot_of[(seq_id, i)] for i in sel]
+        ts = self.transfer_stream
+        ts.wait_stream(torch.cuda.current_stream(self.device))  # new pages may still be read by compute
+        with torch.cuda.stream(ts):
+            for c0 in range(0, len(sel), self.staging_pages):
+                chunk = pages[c0:c0 + self.staging_pages]
+                ids = self._flat_ids(chunk)
+                for w in (0, 1):
+                    for i, s0, n in self._runs(slots[c0:c0 + len(chunk)]):
+                        self._staging[w, i:i + n].copy_(self._arena[w, s0:s0 + n], non_blocking=True)
+                    self._move(False, ids, w)
+            ev = torch.cuda.Event()
+            ev.record(ts)
+        self._pending[seq_id] = dict(kind="prefetch", event=ev, sel=sel, pages=pages, slots=slots)
+        for e in entries:
+            e.state = OffloadState.PREFETCH_INFLIGHT
+            e.transfer_event = ev
+            e.pending_block_indices = list(sel)
+        self._inc_stat('prefetch_blocks', len(sel))
+        return False
+
+    def _apply_prefetch(self, seq_id: int, p: dict) -> None:
+        del self._pending[seq_id]
+        for e in self._entries(seq_id):
+            for idx, page in zip(p["sel"], p["pages"]):
+                e.gpu_block_map[idx] = int(page)
+                e.block_ids[idx] = int(page)
+                e.cpu_k_blocks[idx] = None
+                e.cpu_v_blocks[idx] = None
+            e.transfer_event = None
+            e.pending_block_indices = None
+            self._update_entry_state(e)
+        for idx in p["sel"]:
+            self._slot_of.pop((seq_id, idx), None)
+        self._free_slots.extend(p["slots"])
+        self.pool.cpu_used_bytes = max(0, self.pool.cpu_used_bytes - len(p["sel"]) * 2 * self.num_layers *
+                                       self.page_elems * self.pool.k_cache.element_size())
+        self._inc_stat('prefetch_success')
+
+    def _try_finalize_prefetch(self, seq_id: int, force_sync: bool = False) -> bool:
+        p = self._pending.get(seq_id)
+        if p is None or p["kind"] != "prefetch":
+            return False
+        if not force_sync and not p["event"].query():
+            return False
+        p["event"].synchronize()
+        # host slots are reusable only once the H2D copy has read them
+        self._apply_prefetch(seq_id, p)
+        return True
+
+    def ensure_sequence_blocks_on_gpu(self, seq_id: int, logical_block_indices: Optional[List[int]] = None,
+                                      stream: Optional[torch.cuda.Stream] = None) -> bool:
+        """Make the given pages resident for work queued on ``stream`` (default:
+        the current stream) WITHOUT blocking the host: the prefetch runs on the
+        side stream and ``stream`` waits on its event.  Host slots are recycled
+        when the event has completed (polled by later calls)."""
+        self._try_finalize_offload(seq_id, force_sync=True)
+        entries = self._entries(seq_id)
+        if not entries:
+            return False
+        idx = list(range(len(entries[0].gpu_block_map))) if logical_block_indices is None else logical_block_indices
+        if self.prefetch_sequence_blocks(seq_id, idx):
+            return True
+        p = self._pending.get(seq_id)
+        if p is None or p["kind"] != "prefetch":
+            return False
+        (stream or torch.cuda.current_stream(self.device)).wait_event(p["event"])
+        # the mapping is valid in stream order from here on; only slot reuse waits for the event
+        slots_event = p["event"]
+        self._apply_prefetch(seq_id, dict(p, slots=[]))
+        self._deferred_slots = getattr(self, "_deferred_slots", [])
+        self._deferred_slots.append((slots_event, p["slots"]))
+        self._reclaim_slots()
+        return True
+
+    def _reclaim_slots(self) -> None:
+        keep = []
+        for ev, slots in getattr(self, "_deferred_slots", []):
+            if ev.query():
+                self._free_slots.extend(slots)
+            else:
+                keep.append((ev, slots))
+        self._deferred_slots = keep
+
+    # ---- decode bookkeeping (core/offload.py:780-866) -------------------------
+    def reserve_decode_slot(self, seq_id: int) -> DecodeAppendResult:
+        entries = self._entries(seq_id)
+        if len(entries) != self.num_layers:
+            return DecodeAppendResult(ok=False, retryable=False, reason=f"missing_page_table_entry seq={seq_id}")
+        for e in entries:
+            self._ensure_entry_maps(e)
+            if e.state != OffloadState.ON_GPU or any(int(b) < 0 for b in e.gpu_block_map):
+                return DecodeAppendResult(ok=False, retryable=True,
+                                          reason=f"direct_decode_not_on_gpu seq={seq_id} state={e.state}")
+        seq_len = int(entries[0].seq_len)
+        if any(int(e.seq_len) != seq_len for e in entries):
+            return DecodeAppendResult(ok=False, retryable=False,
+                                      reason=f"direct_decode_inconsistent_seq_len seq={seq_id}")
+        if seq_len % self.pool.B == 0:
+            new = self.pool.allocate_blocks(1)
+            if not new:
+                return DecodeAppendResult(ok=False, retryable=True, reason="direct_decode_expand_alloc_failed")
+            for e in entries:
+                e.block_ids.append(int(new[0]))
+                e.gpu_block_map.append(int(new[0]))
+                e.cpu_k_blocks.append(None)
+                e.cpu_v_blocks.append(None)
+                e.materialized_blocks = len(e.gpu_block_map)
+        return DecodeAppendResult(ok=True)
+
+    def commit_decode_token(self, seq_id: int) -> None:
+        for e in self._entries(seq_id):
+            e.seq_len += 1
+            e.logical_seq_len = int(e.logical_seq_len or e.seq_len - 1) + 1
+
+    def release_sequence(self, seq_id: int):
+        self._try_finalize_offload(seq_id, force_sync=True)
+        self._try_finalize_prefetch(seq_id, force_sync=True)
+        entries = self._entries(seq_id)
+        if entries:
+            self.pool.free_blocks_by_ids([int(b) for b in entries[0].gpu_block_map if int(b) >= 0])
+        for key in [k for k in self._slot_of if k[0] == seq_id]:
+            self._free_slots.append(self._slot_of.pop(key))
+        for l in range(self.num_layers):
+            self.page_table.pop((seq_id, l), None)

@@ -16,7 +16,24 @@
 #include "common.cuh"
 
 namespace bpkv {
+
+struct PrefillTcParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int32_t* bt;
+  const int32_t* cu_q;
+  const int32_t* seqlens_k;
+  void* out;
+  int B, Hq, Hkv, n_rep, tiles_per_req, causal;
+  int64_t page_stride, bt_sb;
+  float scale_log2;
+};
+// tcgen05/TMEM kernel (prefill_tc.cu): head_dim 128; BPKV_ERR_UNSUPPORTED otherwise.
+int prefill_tc_launch(PrefillTcParams& p, int head_dim, int dtype, int max_seqlen_q, bool paged, cudaStream_t st);
+
 namespace {
+
 
 constexpr int kRows = 64;   // packed (token, head) rows per CTA
 constexpr int kKvTile = 64; // KV tokens per tile
@@ -255,7 +272,30 @@ int launch_prefill(PrefillParams& p, int max_seqlen_q, cudaStream_t st) {
 }
 
 template <bool PAGED>
+int try_tc(const PrefillParams& p, int D, int dtype, int max_seqlen_q, cudaStream_t st) {
+  PrefillTcParams t{};
+  t.q = p.q;
+  t.k = p.k;
+  t.v = p.v;
+  t.bt = p.bt;
+  t.cu_q = p.cu_q;
+  t.seqlens_k = p.seqlens_k;
+  t.out = p.out;
+  t.B = p.B;
+  t.Hq = p.Hq;
+  t.Hkv = p.Hkv;
+  t.n_rep = p.n_rep;
+  t.causal = p.causal;
+  t.page_stride = p.page_stride;
+  t.bt_sb = p.bt_sb;
+  t.scale_log2 = p.scale_log2;
+  return prefill_tc_launch(t, D, dtype, max_seqlen_q, PAGED, st);
+}
+
+template <bool PAGED>
 int dispatch_prefill(PrefillParams& p, int D, int dtype, int max_seqlen_q, cudaStream_t st) {
+  const int rc = try_tc<PAGED>(p, D, dtype, max_seqlen_q, st);
+  if (rc != BPKV_ERR_UNSUPPORTED) return rc;
 #define BPKV_PF(TY)                                                              \
   switch (D) {                                                                   \
     case 64: return launch_prefill<TY, 64, PAGED>(p, max_seqlen_q, st);          \

@@ -354,12 +354,197 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+
+# ---------------------------------------------------------------------------
+# Secondary workloads (one JSON line each; the default run is the decode above)
+# ---------------------------------------------------------------------------
+def _events_time(fn, steps, warmup):
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def run_prefill(args):
+    """Config 5, prefill part: 8 requests x 512-token chunks appended into paged KV,
+    causal over past (lognormal(ln 4000, 0.8) clipped to [256, 32768]) + chunk;
+    32 layers, Llama-3.1-8B heads, bf16, tcgen05 kernel."""
+    import torch
+    from unifiedkv_b200.chunked_prefill import paged_chunk_prefill
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(55)
+    nreq, chunk = 8, 512
+    past = np.clip(np.exp(rng.normal(np.log(4000), 0.8, size=nreq)), 256, 32768).astype(np.int64)
+    totals = past + chunk
+    need = (totals + 15) // 16
+    n_pages = int(need.sum()) + 16
+    layers = 1 if getattr(args, "profile_small", False) else LAYERS
+    kp = torch.empty((layers, n_pages, 16, HKV, D), dtype=torch.bfloat16, device=dev).normal_(0, 0.5)
+    vp = torch.empty_like(kp).normal_(0, 0.5)
+    perm = rng.permutation(n_pages).astype(np.int32)
+    bt = np.zeros((nreq, int(need.max())), np.int32)
+    off = 0
+    for b, n in enumerate(need):
+        bt[b, :n] = perm[off:off + n]
+        off += int(n)
+    bt_d = torch.from_numpy(bt).to(dev)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum([chunk] * nreq)]), dtype=torch.int32, device=dev)
+    sk = torch.tensor(totals, dtype=torch.int32, device=dev)
+    qs = [(torch.randn(nreq * chunk, HQ, D, device=dev) * 0.5).to(torch.bfloat16) for _ in range(layers)]
+
+    def step():
+        for l in range(layers):
+            paged_chunk_prefill(qs[l], kp[l], vp[l], bt_d, None, None, D ** -0.5, HQ // HKV, cu_seqlens_q=cu,
+                                seqlens_k=sk, max_seqlen_q=chunk)
+    ms = _events_time(step, args.steps, args.warmup)
+    flops_layer = 4.0 * HQ * D * float(np.sum(chunk * (past + (chunk + 1) / 2.0)))
+    tflops = flops_layer * layers / (ms * 1e-3) / 1e12
+    hbm, tf, kind = _peaks()
+    print(json.dumps({
+        "metric": "paged chunked-prefill attention TFLOP/s (config 5 prefill part)", "value": round(tflops, 2),
+        "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "8 requests x 512-token causal chunks over paged past (lognormal(ln 4000,0.8) "
+                               "clipped [256,32768]), 32 layers, 32q/8kv heads, d128", "past": past.tolist()},
+        "tokens_per_s": round(nreq * chunk / (ms * 1e-3), 1),
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": tf, "unit": "TFLOP/s",
+                     "frac": round(tflops / tf, 4), "peak_source": f"{kind} bf16_tflops (burst)",
+                     "kernel": "prefill_tc_kernel<bf16,paged> (tcgen05, TMEM)",
+                     "note": "algorithmic FLOPs 4*h_q*d*sum(n_q*(past+(n_q+1)/2)); bf16 P is split hi+lo so the "
+                             "tensor pipe executes 1.5x these FLOPs"},
+        "gpu_launches": layers * args.steps,
+    }), flush=True)
+
+
+def run_compress(args):
+    """Config 4: one 32768-token sequence, 8 KV heads, d128, 64-query window over
+    32 q-heads, 32 hot blocks; keep 25% of mid blocks + first 4 + last 8 blocks,
+    compact into fresh pool pages; 32 layers per step."""
+    import torch
+    from tests.golden.inputs import compress_case  # seeded input generator (no oracle)
+    from unifiedkv_b200.compress import SMOOTH_ALWAYS, block_scores, topk_blocks
+    from unifiedkv_b200.pool import write_pages
+    dev = torch.device("cuda", 0)
+    K, V, Q, hot = compress_case(seed=4, h_kv=8, L=32768, d=128, n_rep=4, window=64, hot_blocks=32, sink=64)
+    tk = torch.from_numpy(K).to(dev, torch.bfloat16)
+    tv = torch.from_numpy(V).to(dev, torch.bfloat16)
+    tq = torch.from_numpy(Q).to(dev, torch.bfloat16)
+    layers = 1 if getattr(args, "profile_small", False) else LAYERS
+    Ks = [tk.clone() for _ in range(layers)]  # distinct buffers per layer: no cross-layer L2 reuse
+    Vs = [tv.clone() for _ in range(layers)]
+    sink, obs = 64, 128
+    N = math.ceil((32768 - sink - obs) / 16)
+    k = int(math.floor(0.25 * N))
+    eff = sink + 16 * k + obs
+    n_dst = math.ceil(eff / 16)
+    pool_k = torch.empty((layers, n_dst + 8, 16, 8, 128), dtype=torch.bfloat16, device=dev)
+    pool_v = torch.empty_like(pool_k)
+    dst = torch.arange(n_dst, dtype=torch.int32, device=dev)
+
+    def step():
+        for l in range(layers):
+            sc = block_scores(Ks[l], tq, sink, obs, smooth=SMOOTH_ALWAYS)
+            sel = topk_blocks(sc, k)
+            write_pages(pool_k[l], pool_v[l], Ks[l], Vs[l], dst, sel, k, sink, obs)
+    ms = _events_time(step, args.steps, args.warmup)
+    kmid = 8 * (32768 - sink - obs) * 128 * 2
+    bytes_layer = kmid + tq.numel() * 2 + 2 * 2 * eff * 8 * 128 * 2  # K_mid once, Q, retained K+V read+write
+    flops_layer = 2 * 2.0 * 32 * 64 * (N * 16) * 128  # QK^T, two passes
+    gbs = bytes_layer * layers / (ms * 1e-3) / 1e9
+    hbm, tf, kind = _peaks()
+    print(json.dumps({
+        "metric": "block scoring + top-k + compacting writeback (config 4)", "value": round(ms / layers * 1e3, 2),
+        "unit": "us per layer", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": False, "dtype": "bf16", "data": "synthetic (32 hot blocks at +2 sigma)",
+        "config": {"workload": "L=32768, 8 kv heads, d128, window 64 x 32 q-heads, keep 25% mid + 4 sink + 8 obs "
+                               "blocks, 32 layers", "k_blocks": k, "effective_len": eff},
+        "algorithmic_gbs": round(gbs, 1), "hbm_frac_of_measured": round(gbs / hbm, 4),
+        "tflops": round(flops_layer * layers / (ms * 1e-3) / 1e12, 2),
+        "gpu_launches": 6 * layers * args.steps,
+    }), flush=True)
+
+
+def run_longseq(args, rank, world, local_rank):
+    """Config 3: one sequence of 131072 tokens (8192 pages), 32 layers; at N>1 the
+    page list is split across GPUs and (out, lse) partials merged over NCCL."""
+    import torch
+    import torch.distributed as dist
+    from unifiedkv_b200.multi_gpu import local_range_lens, split_kv_decode, split_pages
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    L, pages = 131072, 8192
+    s, e = split_pages(pages, world)[rank]
+    n_local = e - s
+    layers = 1 if getattr(args, "profile_small", False) else LAYERS
+    g = torch.Generator(device=dev).manual_seed(300 + rank)
+    kp = torch.empty((layers, n_local, 16, HKV, D), dtype=torch.bfloat16, device=dev).normal_(0, 1, generator=g)
+    vp = torch.empty_like(kp).normal_(0, 1, generator=g)
+    gq = torch.Generator(device=dev).manual_seed(299)
+    qs = [(torch.randn(1, HQ, D, device=dev, generator=gq) * 0.5).to(torch.bfloat16) for _ in range(layers)]
+    bt = torch.randperm(n_local, device=dev, generator=g).to(torch.int32)[None]
+    lens = torch.tensor([local_range_lens(L, s, e)], dtype=torch.int32, device=dev)
+    from unifiedkv_b200.page16_native import page16_decode_attention
+
+    def step():
+        for l in range(layers):
+            if world > 1:
+                split_kv_decode(qs[l], kp[l], vp[l], bt, lens, D ** -0.5, HQ // HKV)
+            else:
+                page16_decode_attention(qs[l], kp[l], vp[l], bt, lens, softmax_scale=D ** -0.5, n_rep=HQ // HKV)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if rank != 0:
+        return
+    bytes_step = L * KV_BYTES_PER_TOKEN * layers
+    gbs = bytes_step / (ms * 1e-3) / 1e9
+    hbm, tf, kind = _peaks()
+    print(json.dumps({
+        "metric": "single-sequence 131072-token decode KV-read GB/s (config 3)", "value": round(gbs, 1),
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "strong", "dtype": "bf16", "data": "synthetic N(0,1) K/V",
+        "config": {"workload": "B=1, 131072 tokens (8192 pages) split over GPUs, 32 layers, 32q/8kv, d128",
+                   "parallelism": f"split-KV x{world} + NCCL all-gather of (out, lse)"},
+        "ms_per_layer": round(ms / layers, 4), "tokens_per_s": round(1000.0 / ms, 2),
+        "hbm_frac_of_measured_per_gpu": round(gbs / world / hbm, 4),
+    }), flush=True)
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "compress", "longseq"],
+                    help="decode = headline config 2; the others print their own metric line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-small", action="store_true",
                     help="ncu case: 1 layer, pool of only the needed pages (same per-launch work)")
@@ -376,7 +561,12 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
-        run_ours(args, rank, world, local_rank)
+        if args.workload == "decode":
+            run_ours(args, rank, world, local_rank)
+        elif args.workload == "longseq":
+            run_longseq(args, rank, world, local_rank)
+        elif rank == 0:
+            run_prefill(args) if args.workload == "prefill" else run_compress(args)
     finally:
         if world > 1:
             import torch.distributed as dist

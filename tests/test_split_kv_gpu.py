@@ -1,0 +1,95 @@
+"""Split-KV decode of one long sequence: the page list is cut into per-rank
+ranges, each range is decoded with lse_out, and the (out, lse) partials are
+merged by the LSE-combine kernel.  On one GPU the ranks are emulated (the
+merge input is stacked locally, as the NCCL all-gather would deliver it); with
+two or more GPUs visible the real path runs as NCCL ranks."""
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(dev, L=20000, hq=32, hkv=8, d=128, seed=3):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    n_pages = math.ceil(L / 16)
+    kc = torch.randn(n_pages, 16, hkv, d, generator=g, device=dev).to(torch.bfloat16)
+    vc = torch.randn(n_pages, 16, hkv, d, generator=g, device=dev).to(torch.bfloat16)
+    q = (torch.randn(1, hq, d, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+    return q, kc, vc, n_pages
+
+
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_split_kv_emulated_ranks(cuda, world):
+    from unifiedkv_b200.multi_gpu import local_range_lens, split_pages
+    from unifiedkv_b200.page16_native import lse_combine, page16_decode_attention
+    L = 20000
+    q, kc, vc, n_pages = _case(cuda, L)
+    full_lse = torch.empty(1, 32, dtype=torch.float32, device=cuda)
+    full = page16_decode_attention(q, kc, vc, torch.arange(n_pages, dtype=torch.int32, device=cuda)[None],
+                                   torch.tensor([L], dtype=torch.int32, device=cuda), softmax_scale=128 ** -0.5,
+                                   n_rep=4, lse_out=full_lse)
+    parts, lses = [], []
+    for s, e in split_pages(n_pages, world):
+        lse = torch.empty(1, 32, dtype=torch.float32, device=cuda)
+        o = page16_decode_attention(q, kc[s:e], vc[s:e], torch.arange(e - s, dtype=torch.int32, device=cuda)[None],
+                                    torch.tensor([local_range_lens(L, s, e)], dtype=torch.int32, device=cuda),
+                                    softmax_scale=128 ** -0.5, n_rep=4, lse_out=lse)
+        parts.append(o.float().reshape(32, 128))
+        lses.append(lse.reshape(32))
+    merged, mlse = lse_combine(torch.stack(parts), torch.stack(lses), torch.bfloat16, return_lse=True)
+    # partials pass through bf16 outputs of each range: allow 2 bf16 ulps of |out| + 2e-3
+    diff = (merged.float() - full.float().reshape(32, 128)).abs()
+    assert (diff - 2 ** -7 * full.float().reshape(32, 128).abs()).max().item() < 2e-3
+    assert (mlse - full_lse.reshape(32)).abs().max().item() < 1e-3
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, q_out):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        from unifiedkv_b200.multi_gpu import local_range_lens, split_kv_decode, split_pages
+        from unifiedkv_b200.page16_native import page16_decode_attention
+        L = 20000
+        q, kc, vc, n_pages = _case(dev, L)  # identical data on every rank (same seed)
+        s, e = split_pages(n_pages, world)[rank]
+        out = split_kv_decode(q, kc[s:e], vc[s:e], torch.arange(e - s, dtype=torch.int32, device=dev)[None],
+                              torch.tensor([local_range_lens(L, s, e)], dtype=torch.int32, device=dev),
+                              128 ** -0.5, 4)
+        full = page16_decode_attention(q, kc, vc, torch.arange(n_pages, dtype=torch.int32, device=dev)[None],
+                                       torch.tensor([L], dtype=torch.int32, device=dev), softmax_scale=128 ** -0.5,
+                                       n_rep=4)
+        d = (out.float() - full.float()).abs() - 2 ** -8 * full.float().abs()
+        q_out.put((rank, float(d.max().item())))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_split_kv_nccl_two_ranks(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    qq = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_nccl_worker, args=(r, 2, port, qq)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(qq.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(err < 2e-3 for _, err in res), res

@@ -23,11 +23,12 @@ from .pool import write_pages
 def paged_chunk_prefill(q_chunk: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                         block_table: torch.Tensor, past_lens, chunk_lens, softmax_scale: float, n_rep: int,
                         causal: bool = True, cu_seqlens_q: Optional[torch.Tensor] = None,
-                        seqlens_k: Optional[torch.Tensor] = None) -> torch.Tensor:
+                        seqlens_k: Optional[torch.Tensor] = None, max_seqlen_q: Optional[int] = None) -> torch.Tensor:
     """q_chunk: [total_q, h_q, d] (chunks of all requests packed); k/v_cache: one
     layer's pool view [N, 16, h_kv, d]; block_table: int32 [B, max_blocks];
     past_lens / chunk_lens: per-request lists (or pass device tensors
-    cu_seqlens_q [B+1] and seqlens_k [B] = past + chunk directly)."""
+    cu_seqlens_q [B+1] and seqlens_k [B] = past + chunk directly, with
+    max_seqlen_q the longest chunk; it sizes the grid)."""
     total, h_q, d = [int(x) for x in q_chunk.shape]
     h_kv = int(k_cache.shape[2])
     if h_q != h_kv * int(n_rep) or int(k_cache.shape[1]) != 16 or int(k_cache.shape[3]) != d:
@@ -49,7 +50,7 @@ def paged_chunk_prefill(q_chunk: torch.Tensor, k_cache: torch.Tensor, v_cache: t
         seqlens_k = torch.tensor([p + c for p, c in zip(past_lens, chunk_lens)], dtype=torch.int32).to(dev, non_blocking=True)
         max_q = max(chunk_lens, default=0)
     else:
-        max_q = total
+        max_q = int(max_seqlen_q) if max_seqlen_q is not None else total
     q_chunk = q_chunk.contiguous()
     bt = block_table.to(torch.int32).contiguous()
     out = torch.empty_like(q_chunk)

@@ -226,37 +226,54 @@ __global__ void __launch_bounds__(kScoreWarps * 32) score_tile_kernel(ScoreParam
   }
 }
 
+// One warp per window row: (m, l) over the row's chunks, coalesced, fixed order
+// (lane-strided partial then a fixed shuffle tree).
 __global__ void stats_reduce_kernel(const float2* ml_part, float2* ml, int nrows, int n_chunks) {
-  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
   if (r >= nrows) return;
   const float2* src = ml_part + static_cast<int64_t>(r) * n_chunks;
   float m = -INFINITY;
-  for (int c = 0; c < n_chunks; ++c) m = fmaxf(m, src[c].x);
+  for (int c = lane; c < n_chunks; c += 32) m = fmaxf(m, src[c].x);
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   float l = 0.f;
-  for (int c = 0; c < n_chunks; ++c) l += src[c].y * exp2f(src[c].x - m);
-  ml[r] = make_float2(m, l);
+  for (int c = lane; c < n_chunks; c += 32) l += src[c].y * exp2f(src[c].x - m);
+  for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+  if (lane == 0) ml[r] = make_float2(m, l);
 }
 
-// raw block n = sum_{t in block} max_g headmax[g][t]; then optional max-pool 3.
-__global__ void block_reduce_kernel(const float* headmax, float* out, int Hkv, int Tm, int N, int smooth) {
-  const int n = blockIdx.x * blockDim.x + threadIdx.x;
-  if (n >= N) return;
-  auto raw = [&](int b) {
-    float s = 0.f;
-    for (int t = b * kPage; t < b * kPage + kPage; ++t) {
-      float mx = -INFINITY;
-      for (int g = 0; g < Hkv; ++g) mx = fmaxf(mx, headmax[static_cast<int64_t>(g) * Tm + t]);
-      s += mx;
-    }
-    return s;
-  };
-  float v = raw(n);
-  const bool pool = smooth == 2 || (smooth == 1 && N >= 3);
-  if (pool) {
-    if (n > 0) v = fmaxf(v, raw(n - 1));
-    if (n + 1 < N) v = fmaxf(v, raw(n + 1));
+// Block scores: a CTA of 256 threads covers kBlkPerCta blocks plus one halo
+// block on each side.  Thread = token: max over kv heads (coalesced rows of
+// headmax), 16-token sums by a fixed shuffle tree, then optional max-pool 3.
+constexpr int kBlkPerCta = 14;  // (14 + 2) blocks x 16 tokens = 256 threads
+__global__ void __launch_bounds__(256) block_reduce_kernel(const float* headmax, float* out, int Hkv, int Tm, int N,
+                                                           int smooth) {
+  __shared__ float raw[kBlkPerCta + 2];
+  const int b0 = blockIdx.x * kBlkPerCta - 1;  // first (halo) block
+  const int t = threadIdx.x;
+  const int blk = b0 + t / kPage;
+  const int tok = blk * kPage + (t % kPage);
+  float v = 0.f;
+  if (blk >= 0 && blk < N) {
+    float mx = -INFINITY;
+    for (int g = 0; g < Hkv; ++g) mx = fmaxf(mx, headmax[static_cast<int64_t>(g) * Tm + tok]);
+    v = mx;
   }
-  out[n] = v;
+  for (int o = 1; o < kPage; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((t % kPage) == 0) raw[t / kPage] = v;
+  __syncthreads();
+  if (t < kBlkPerCta) {
+    const int n = b0 + 1 + t;
+    if (n < N) {
+      float r = raw[t + 1];
+      const bool pool = smooth == 2 || (smooth == 1 && N >= 3);
+      if (pool) {
+        if (n > 0) r = fmaxf(r, raw[t]);
+        if (n + 1 < N) r = fmaxf(r, raw[t + 2]);
+      }
+      out[n] = r;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -424,9 +441,9 @@ int launch_score(ScoreParams& p, float* out, int N, int smooth, cudaStream_t st)
   dim3 grid(p.n_chunks, p.Hkv);
   k1<<<grid, kScoreWarps * 32, smem, st>>>(p);
   const int nrows = p.Hq * p.Wp;
-  stats_reduce_kernel<<<(nrows + 255) / 256, 256, 0, st>>>(p.ml_part, p.ml, nrows, p.n_chunks);
+  stats_reduce_kernel<<<(nrows * 32 + 255) / 256, 256, 0, st>>>(p.ml_part, p.ml, nrows, p.n_chunks);
   k2<<<grid, kScoreWarps * 32, smem, st>>>(p);
-  block_reduce_kernel<<<(N + 127) / 128, 128, 0, st>>>(p.headmax, out, p.Hkv, p.Tm, N, smooth);
+  block_reduce_kernel<<<(N + kBlkPerCta - 1) / kBlkPerCta, 256, 0, st>>>(p.headmax, out, p.Hkv, p.Tm, N, smooth);
   BPKV_RETURN_LAUNCH("block_score_launch");
 }
 

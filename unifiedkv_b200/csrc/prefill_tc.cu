@@ -44,8 +44,9 @@ constexpr int kD = 128, kBM = 128, kBN = 64, kDB = kD / 64;
 constexpr int kQBytes = kDB * kBM * 128;       // 32 KB
 constexpr int kKVBytes = kDB * kBN * 128;      // 16 KB per K or V tile
 constexpr int kPBytes = kBM * 128;             // 16 KB (64 tokens per row)
-constexpr int kSmemBytes = kQBytes + 4 * kKVBytes + 2 * kPBytes + 1024 /*align*/ + 64;
-constexpr uint32_t kTmemCols = 256;            // S: [0,64), O tile: [64,192)
+constexpr int kNBuf = 4;                       // K/V ring depth
+constexpr int kSmemBytes = kQBytes + 2 * kNBuf * kKVBytes + 2 * kPBytes + 1024 /*align*/ + 64;
+constexpr uint32_t kTmemCols = 512;            // S0 [0,64) S1 [64,128) O0 [128,256) O1 [256,384)
 
 __device__ __forceinline__ uint32_t sw_off(int row, int chunk) {  // chunk 0..7 inside a 128-B row
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
@@ -56,13 +57,12 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* qs = smem;
-  uint8_t* ks = qs + kQBytes;            // 2 buffers
-  uint8_t* vs = ks + 2 * kKVBytes;       // 2 buffers
-  uint8_t* ph = vs + 2 * kKVBytes;
+  uint8_t* ks = qs + kQBytes;            // kNBuf buffers
+  uint8_t* vs = ks + kNBuf * kKVBytes;   // kNBuf buffers
+  uint8_t* ph = vs + kNBuf * kKVBytes;
   uint8_t* pl = ph + kPBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pl + kPBytes);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2);
-  const uint32_t bar_s = smem_u32(&bars[0]), bar_o = smem_u32(&bars[1]);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pl + kPBytes);  // S0, S1, O0, O1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
 
   const int b = blockIdx.x / p.tiles_per_req;
   const int qt = blockIdx.x % p.tiles_per_req;
@@ -83,8 +83,7 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    tc::mbar_init(bar_s, 1);
-    tc::mbar_init(bar_o, 1);
+    for (int i = 0; i < 4; ++i) tc::mbar_init(smem_u32(&bars[i]), 1);
     tc::fence_mbar_init();
   }
 
@@ -121,18 +120,25 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
       cp_async16(smem_u32(vb + so), ok ? (const void*)(vg + off + ch * 8) : (const void*)vg, ok);
     }
   };
-  if (n_tiles > 0) load_kv(0, 0);
-  cp_async_commit();
+  // prologue: tiles 0..2 in flight (one commit group per tile, empty groups past the end)
+#pragma unroll
+  for (int t = 0; t < kNBuf - 1; ++t) {
+    if (t < n_tiles) load_kv(t, t);
+    cp_async_commit();
+  }
 
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_o = tmem + 64;
   const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   constexpr bool kBf16 = SplitP<T>::value;
   const uint32_t id_s = tc::idesc_f16(kBf16, false, false, kBM, kBN);
   const uint32_t id_o = tc::idesc_f16(kBf16, false, true, kBM, kD);
+  auto t_s = [&](int j) { return tmem + static_cast<uint32_t>((j & 1) * kBN); };
+  auto t_o = [&](int j) { return tmem + 2u * kBN + static_cast<uint32_t>((j & 1) * kD); };
+  auto bar_s = [&](int j) { return smem_u32(&bars[j & 1]); };
+  auto bar_o = [&](int j) { return smem_u32(&bars[2 + (j & 1)]); };
 
   // row of this thread
   const int row = tid;
@@ -141,41 +147,73 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
   float acc[kD];
 #pragma unroll
   for (int i = 0; i < kD; ++i) acc[i] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;
+  float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
   bool failed = false;
 
-  for (int it = 0; it < n_tiles; ++it) {
-    const int buf = it & 1;
-    if (it + 1 < n_tiles) load_kv(it + 1, buf ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
-    tc::fence_proxy_async_smem();  // cp.async data -> visible to the tensor core
-    __syncthreads();
-
-    // ---- S = Q K^T (8 k-steps of 16 over head_dim) ----
-    if (tid == 0) {
-      tc::tc_fence_after();
-      const uint32_t qa = smem_u32(qs), kb = smem_u32(ks + buf * kKVBytes);
+  // S(j) = Q K(j)^T into S buffer j&1 (issued by one thread)
+  auto issue_s = [&](int j) {
+    tc::tc_fence_after();
+    const uint32_t qa = smem_u32(qs), kb = smem_u32(ks + (j % kNBuf) * kKVBytes);
 #pragma unroll
-      for (int kk = 0; kk < kD / 16; ++kk) {
-        const uint32_t koff = (kk & 3) * 32;
-        const uint64_t ad = tc::smem_desc_sw128(qa + (kk >> 2) * (kBM * 128) + koff, 16, 1024);
-        const uint64_t bd = tc::smem_desc_sw128(kb + (kk >> 2) * (kBN * 128) + koff, 16, 1024);
-        tc::mma_f16(t_s, ad, bd, id_s, kk > 0 ? 1u : 0u);
-      }
-      tc::mma_commit(bar_s);
+    for (int kk = 0; kk < kD / 16; ++kk) {
+      const uint32_t koff = (kk & 3) * 32;
+      const uint64_t ad = tc::smem_desc_sw128(qa + (kk >> 2) * (kBM * 128) + koff, 16, 1024);
+      const uint64_t bd = tc::smem_desc_sw128(kb + (kk >> 2) * (kBN * 128) + koff, 16, 1024);
+      tc::mma_f16(t_s(j), ad, bd, id_s, kk > 0 ? 1u : 0u);
     }
-    const bool ok_s = tc::mbar_wait(bar_s, it & 1);
+    tc::mma_commit(bar_s(j));
+  };
+  // O(j) = P(j) V(j) into O buffer j&1 (bf16: hi part then lo part)
+  auto issue_o = [&](int j) {
+    tc::tc_fence_after();
+    const uint32_t vb = smem_u32(vs + (j % kNBuf) * kKVBytes);
+    const int parts = kBf16 ? 2 : 1;
+    for (int part = 0; part < parts; ++part) {
+      const uint32_t pa = smem_u32(part == 0 ? ph : pl);
+#pragma unroll
+      for (int kk = 0; kk < kBN / 16; ++kk) {
+        const uint64_t ad = tc::smem_desc_sw128(pa + kk * 32, 16, 1024);
+        const uint64_t bd = tc::smem_desc_sw128(vb + kk * 16 * 128, kBN * 128, 1024);
+        tc::mma_f16(t_o(j), ad, bd, id_o, (part > 0 || kk > 0) ? 1u : 0u);
+      }
+    }
+    tc::mma_commit(bar_o(j));
+  };
+  // acc = acc * alpha(j) + O(j)
+  auto fold = [&](int j, float alpha) {
+#pragma unroll
+    for (int c0 = 0; c0 < kD; c0 += 32) {
+      float o[32];
+      tc::tmem_ld32(t_o(j) + lane_base + c0, o);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[c0 + i] = acc[c0 + i] * alpha + o[i];
+    }
+  };
+
+  if (n_tiles > 0) {
+    cp_async_wait<kNBuf - 2>();  // tile 0 resident
+    tc::fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) issue_s(0);
+  }
+
+  for (int it = 0; it < n_tiles; ++it) {
+    // [A] tile it+1 resident -> S(it+1) can start while this tile's softmax runs
+    cp_async_wait<kNBuf - 3>();
+    tc::fence_proxy_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && it + 1 < n_tiles) issue_s(it + 1);
+
+    const bool ok_s = tc::mbar_wait(bar_s(it), (it >> 1) & 1);
     if (__syncthreads_or(!ok_s)) {
       failed = true;
       break;
     }
     tc::tc_fence_after();
-
-    // ---- softmax on this thread's row ----
     float s[kBN];
-    tc::tmem_ld32(t_s + lane_base, s);
-    tc::tmem_ld32(t_s + lane_base + 32, s + 32);
+    tc::tmem_ld32(t_s(it) + lane_base, s);
+    tc::tmem_ld32(t_s(it) + lane_base + 32, s + 32);
     const int tbase = it * kBN;
     float mx = -INFINITY;
 #pragma unroll
@@ -187,6 +225,20 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
     const float m_use = m_new == -INFINITY ? 0.f : m_new;
     const float alpha = fast_exp2(m_run - m_use);
     m_run = m_new;
+
+    // O(it-1) done: fold it, free its K/V buffer for tile it+3 and the P buffer
+    if (it > 0) {
+      const bool ok_o = tc::mbar_wait(bar_o(it - 1), ((it - 1) >> 1) & 1);
+      if (__syncthreads_or(!ok_o)) {
+        failed = true;
+        break;
+      }
+      tc::tc_fence_after();
+      fold(it - 1, alpha_prev);
+    }
+    if (it + kNBuf - 1 < n_tiles) load_kv(it + kNBuf - 1, (it + kNBuf - 1) % kNBuf);
+    cp_async_commit();
+
     float sum = 0.f;
 #pragma unroll
     for (int c = 0; c < kBN; c += 8) {
@@ -202,41 +254,21 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
       if (kBf16) *reinterpret_cast<uint4*>(pl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
     l_run = l_run * alpha + sum;
+    alpha_prev = alpha;
     tc::fence_proxy_async_smem();  // P stores -> visible to the tensor core
     tc::tc_fence_before();
-    __syncthreads();
-
-    // ---- O_tile = P V (4 k-steps of 16 tokens; bf16: hi part then lo part) ----
-    if (tid == 0) {
-      tc::tc_fence_after();
-      const uint32_t vb = smem_u32(vs + buf * kKVBytes);
-      const int parts = kBf16 ? 2 : 1;
-      for (int part = 0; part < parts; ++part) {
-        const uint32_t pa = smem_u32(part == 0 ? ph : pl);
-#pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk) {
-          const uint64_t ad = tc::smem_desc_sw128(pa + kk * 32, 16, 1024);
-          const uint64_t bd = tc::smem_desc_sw128(vb + kk * 16 * 128, kBN * 128, 1024);
-          tc::mma_f16(t_o, ad, bd, id_o, (part > 0 || kk > 0) ? 1u : 0u);
-        }
-      }
-      tc::mma_commit(bar_o);
-    }
-    const bool ok_o = tc::mbar_wait(bar_o, it & 1);
+    __syncthreads();  // [B]
+    if (tid == 0) issue_o(it);
+  }
+  if (!failed && n_tiles > 0) {
+    const int last = n_tiles - 1;
+    const bool ok_o = tc::mbar_wait(bar_o(last), (last >> 1) & 1);
     if (__syncthreads_or(!ok_o)) {
       failed = true;
-      break;
+    } else {
+      tc::tc_fence_after();
+      fold(last, alpha_prev);
     }
-    tc::tc_fence_after();
-#pragma unroll
-    for (int c0 = 0; c0 < kD; c0 += 32) {
-      float o[32];
-      tc::tmem_ld32(t_o + lane_base + c0, o);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) acc[c0 + i] = acc[c0 + i] * alpha + o[i];
-    }
-    tc::tc_fence_before();
-    __syncthreads();  // S/O TMEM, P and this K/V buffer are reused next iteration
   }
   cp_async_wait<0>();
 

@@ -96,3 +96,39 @@ def test_paged_chunk_prefill(cuda, past, chunk):
         ref = chunk_attention(qn[qo:qo + chunk[b]], kb, vb)
         assert _err(out[qo:qo + chunk[b]], ref, dtype) < 2e-3
         qo += chunk[b]
+
+
+def test_paged_prefill_stale_nan_rows(cuda):
+    """Pool rows past each request's length hold NaN: they must not reach the
+    output (the tensor-core kernel loads whole pages and zeroes those rows)."""
+    from unifiedkv_b200.chunked_prefill import paged_chunk_prefill
+    hq, hkv, d, dtype = 32, 8, 128, torch.bfloat16
+    past, chunk = [100, 37, 0], [60, 200, 17]
+    totals = [p + c for p, c in zip(past, chunk)]
+    need = [math.ceil(t / 16) for t in totals]
+    n_pages = sum(need)
+    g = torch.Generator(device=cuda).manual_seed(5)
+    kc = torch.randn(n_pages, 16, hkv, d, generator=g, device=cuda).to(dtype)
+    vc = torch.randn(n_pages, 16, hkv, d, generator=g, device=cuda).to(dtype)
+    bt = np.zeros((3, max(need)), np.int32)
+    off = 0
+    for b in range(3):
+        bt[b, :need[b]] = np.arange(off, off + need[b])
+        last = off + need[b] - 1
+        r = totals[b] % 16
+        if r:
+            kc[last, r:] = float("nan")
+            vc[last, r:] = float("nan")
+        off += need[b]
+    q = torch.randn(sum(chunk), hq, d, generator=g, device=cuda).to(dtype)
+    out = paged_chunk_prefill(q, kc, vc, torch.from_numpy(bt).to(cuda), past, chunk, d ** -0.5, 4)
+    out = out.float().cpu().numpy()
+    assert np.isfinite(out).all()
+    qn = q.float().cpu().numpy()
+    qo = 0
+    for b in range(3):
+        kb = kc[bt[b, :need[b]]].reshape(-1, hkv, d)[:totals[b]].float().cpu().numpy()
+        vb = vc[bt[b, :need[b]]].reshape(-1, hkv, d)[:totals[b]].float().cpu().numpy()
+        ref = chunk_attention(qn[qo:qo + chunk[b]], kb, vb)
+        assert _err(out[qo:qo + chunk[b]], ref, dtype) < 2e-3
+        qo += chunk[b]

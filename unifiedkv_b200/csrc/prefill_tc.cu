@@ -1,25 +1,30 @@
 // Paged chunked-prefill / varlen attention on the 5th-generation tensor cores
 // (tcgen05.mma with TMEM accumulators), sm_100a, head_dim 128, bf16 / fp16.
 //
-// Same semantics as prefill.cu (causal, bottom-right aligned; K/V gathered
-// from 16-token pages through the block table, or dense varlen).  Per CTA:
+// Same semantics as prefill.cu (causal, bottom-right aligned; K/V read from
+// 16-token pages through the block table, or dense varlen).  Per CTA:
 //   * 128 accumulator rows = 128/n_rep query tokens x the n_rep query heads of
-//     one KV head (a GQA group shares every K/V tile), 4 warps, thread i owns
-//     row i (= TMEM lane i), so the softmax needs no shuffles;
-//   * K/V tiles of 64 tokens are gathered with 16-byte cp.async into the
-//     128-byte-swizzled layout the UMMA descriptors describe
-//     ([64-column block][token][128 B], chunk ^= row & 7, 1024-byte aligned),
-//     double buffered; Q uses the same layout;
-//   * S = Q K^T: one elected thread issues 8 tcgen05.mma (M128 N64 K16, both
-//     operands K-major) into TMEM columns [0,64), commit -> mbarrier;
-//   * the 128 threads pull their S row with tcgen05.ld, apply the causal mask
-//     and online softmax (exp2 domain) and store P to shared memory as
-//     bf16 hi + lo parts (fp16: one part) in the K-major swizzled layout;
-//   * O_tile = P V: tcgen05.mma M128 N128 K16 with V as an MN-major operand
-//     (the same [64-d block][token] tiles), into TMEM columns [64,192);
-//     threads fold it into register accumulators with the softmax rescale.
-// Every mbarrier wait is bounded; on a timeout the CTA abandons its tile,
-// writes NaN rows and still frees its TMEM.
+//     one KV head (a GQA group shares every K/V tile); 4 warps, thread i owns
+//     row i (= TMEM lane i), so the softmax needs no shuffles.
+//   * K/V tiles of 64 tokens (4 pages) land in a 4-deep shared-memory ring in
+//     the 128-byte-swizzled layout of the UMMA descriptors
+//     ([64-column block][token][128 B], 16-B chunk ^= token & 7).  Paged K/V
+//     come by TMA (cp.async.bulk.tensor, 4-D tensor map over the pool layer,
+//     one 16x64 box per page and half of head_dim), issued by one thread and
+//     tracked by transaction bytes on a per-buffer mbarrier; dense varlen K/V
+//     come by 16-byte cp.async that arrive on the same mbarriers.
+//   * S(j) = Q K(j)^T: M128 N64 K16 tcgen05.mma x 8 into one of two TMEM S
+//     buffers; S(j+1) is issued before the softmax of tile j runs.
+//   * softmax with a lazily updated reference max (log2 domain): P stays
+//     <= 2^8, so O only has to be rescaled in TMEM when a row max grows by more
+//     than 8; P goes to shared memory as bf16 hi + lo parts (fp16: one part).
+//   * O += P(j) V(j): M128 N128 K16 with V as an MN-major operand (the same
+//     tiles), accumulated in TMEM across all tiles; read once at the end.
+// All waits are bounded; on a timeout the CTA stops, writes NaN rows and
+// still frees its TMEM.  No TMA multicast is used (the loads read this GPU's
+// own pool only).
+#include <cuda.h>
+
 #include "common.cuh"
 #include "tcgen05.cuh"
 
@@ -45,15 +50,51 @@ constexpr int kQBytes = kDB * kBM * 128;       // 32 KB
 constexpr int kKVBytes = kDB * kBN * 128;      // 16 KB per K or V tile
 constexpr int kPBytes = kBM * 128;             // 16 KB (64 tokens per row)
 constexpr int kNBuf = 4;                       // K/V ring depth
-constexpr int kSmemBytes = kQBytes + 2 * kNBuf * kKVBytes + 2 * kPBytes + 1024 /*align*/ + 64;
-constexpr uint32_t kTmemCols = 512;            // S0 [0,64) S1 [64,128) O0 [128,256) O1 [256,384)
+constexpr int kMaxPagesSmem = 4096;            // block-table entries staged in shared memory
+constexpr int kSmemBytes = kQBytes + 2 * kNBuf * kKVBytes + 2 * kPBytes + 1024 /*align*/ + 128 + 4 * kMaxPagesSmem;
+constexpr uint32_t kTmemCols = 256;            // S0 [0,64) S1 [64,128) O [128,256)
+constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 256 between rescales
+
+struct __align__(64) TcKernelArgs {
+  CUtensorMap tmap_k;  // paged only
+  CUtensorMap tmap_v;
+  PrefillTcParams p;
+};
 
 __device__ __forceinline__ uint32_t sw_off(int row, int chunk) {  // chunk 0..7 inside a 128-B row
   return static_cast<uint32_t>(row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1, int c2, int c3,
+                                            uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+// Arrive on `bar` once all of this thread's prior cp.async copies have landed.
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
+      "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]), "f"(v[9]),
+      "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]), "f"(v[18]),
+      "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]),
+      "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+}
+
 template <typename T, bool PAGED>
-__global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
+__global__ void __launch_bounds__(128, 1) prefill_tc_kernel(const __grid_constant__ TcKernelArgs args) {
+  const PrefillTcParams& p = args.p;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* qs = smem;
@@ -61,8 +102,10 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
   uint8_t* vs = ks + kNBuf * kKVBytes;   // kNBuf buffers
   uint8_t* ph = vs + kNBuf * kKVBytes;
   uint8_t* pl = ph + kPBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pl + kPBytes);  // S0, S1, O0, O1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(pl + kPBytes);  // kv[4], s[2], o[2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  int* s_fail = reinterpret_cast<int*>(tmem_slot + 1);
+  int* s_pages = reinterpret_cast<int*>(bars + 16);  // this request's block-table row (paged)
 
   const int b = blockIdx.x / p.tiles_per_req;
   const int qt = blockIdx.x % p.tiles_per_req;
@@ -77,13 +120,18 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
   const T* qg = reinterpret_cast<const T*>(p.q);
   const T* kg = reinterpret_cast<const T*>(p.k);
   const T* vg = reinterpret_cast<const T*>(p.v);
+  auto bar_kv = [&](int t) { return smem_u32(&bars[t % kNBuf]); };
+  auto bar_s = [&](int j) { return smem_u32(&bars[4 + (j & 1)]); };
+  auto bar_o = [&](int j) { return smem_u32(&bars[6 + (j & 1)]); };
 
   if (warp == 0) {
     tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) tc::mbar_init(smem_u32(&bars[i]), 1);
+    for (int i = 0; i < 4; ++i) tc::mbar_init(smem_u32(&bars[i]), PAGED ? 1u : 128u);
+    for (int i = 4; i < 8; ++i) tc::mbar_init(smem_u32(&bars[i]), 1u);
+    *s_fail = 0;
     tc::fence_mbar_init();
   }
 
@@ -95,63 +143,64 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
     const T* src = qg + (static_cast<int64_t>(q0 + tok) * p.Hq + hkv * p.n_rep + r) * kD + ch * 8;
     cp_async16(smem_u32(qs + (ch >> 3) * (kBM * 128) + sw_off(m, ch & 7)), ok ? (const void*)src : (const void*)qg, ok);
   }
+  cp_async_commit();
   const int last_tok = min(tok0 + TQ, nq) - 1;
   const int kv_end = p.causal ? min(sk, sk - nq + last_tok + 1) : sk;
   const int n_tiles = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
 
-  auto load_kv = [&](int tile, int buf) {
-    uint8_t* kb = ks + buf * kKVBytes;
-    uint8_t* vb = vs + buf * kKVBytes;
-    for (int ci = tid; ci < kBN * (kD / 8); ci += 128) {
-      const int tt = ci / (kD / 8), ch = ci % (kD / 8);
-      const int t = tile * kBN + tt;
-      const bool ok = t < kv_end;
-      int64_t off = 0;
-      if (ok) {
-        if (PAGED) {
-          const int page = __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + t / kPage);
-          off = static_cast<int64_t>(page) * p.page_stride + (static_cast<int64_t>(t % kPage) * p.Hkv + hkv) * kD;
-        } else {
-          off = (static_cast<int64_t>(q0 + t) * p.Hkv + hkv) * kD;
-        }
-      }
-      const uint32_t so = (ch >> 3) * (kBN * 128) + sw_off(tt, ch & 7);
-      cp_async16(smem_u32(kb + so), ok ? (const void*)(kg + off + ch * 8) : (const void*)kg, ok);
-      cp_async16(smem_u32(vb + so), ok ? (const void*)(vg + off + ch * 8) : (const void*)vg, ok);
-    }
-  };
-  // prologue: tiles 0..2 in flight (one commit group per tile, empty groups past the end)
-#pragma unroll
-  for (int t = 0; t < kNBuf - 1; ++t) {
-    if (t < n_tiles) load_kv(t, t);
-    cp_async_commit();
+  if constexpr (PAGED) {
+    const int np = min((kv_end + kPage - 1) / kPage, kMaxPagesSmem);
+    for (int i = tid; i < np; i += 128) s_pages[i] = __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + i);
   }
-
   tc::tc_fence_before();
-  __syncthreads();
+  __syncthreads();  // barriers initialised, TMEM address published, block-table row staged
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+
+  // K/V tile t -> ring buffer t % kNBuf
+  auto load_tile = [&](int t) {
+    const int buf = t % kNBuf;
+    if constexpr (PAGED) {
+      if (tid == 0) {
+        const int pg0 = t * (kBN / kPage);
+        int npg = 0;
+        for (int pg = 0; pg < kBN / kPage; ++pg)
+          if ((pg0 + pg) * kPage < kv_end) ++npg;
+        mbar_expect_tx(bar_kv(t), static_cast<uint32_t>(npg * 2 * kDB * kPage * 128));
+        for (int pg = 0; pg < npg; ++pg) {
+          const int idx = pg0 + pg;
+          const int page = idx < kMaxPagesSmem ? s_pages[idx] : __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + idx);
+#pragma unroll
+          for (int db = 0; db < kDB; ++db) {
+            const uint32_t off = buf * kKVBytes + db * (kBN * 128) + pg * kPage * 128;
+            tma_load_4d(smem_u32(ks + off), &args.tmap_k, db * 64, hkv, 0, page, bar_kv(t));
+            tma_load_4d(smem_u32(vs + off), &args.tmap_v, db * 64, hkv, 0, page, bar_kv(t));
+          }
+        }
+      }
+    } else {
+      for (int ci = tid; ci < kBN * (kD / 8); ci += 128) {
+        const int tt = ci / (kD / 8), ch = ci % (kD / 8);
+        const int tk = t * kBN + tt;
+        const bool ok = tk < kv_end;
+        const int64_t off = ok ? (static_cast<int64_t>(q0 + tk) * p.Hkv + hkv) * kD + ch * 8 : 0;
+        const uint32_t so = buf * kKVBytes + (ch >> 3) * (kBN * 128) + sw_off(tt, ch & 7);
+        cp_async16(smem_u32(ks + so), ok ? (const void*)(kg + off) : (const void*)kg, ok);
+        cp_async16(smem_u32(vs + so), ok ? (const void*)(vg + off) : (const void*)vg, ok);
+      }
+      cp_async_arrive(bar_kv(t));
+    }
+  };
+  for (int t = 0; t < kNBuf - 1 && t < n_tiles; ++t) load_tile(t);
+
   constexpr bool kBf16 = SplitP<T>::value;
   const uint32_t id_s = tc::idesc_f16(kBf16, false, false, kBM, kBN);
   const uint32_t id_o = tc::idesc_f16(kBf16, false, true, kBM, kD);
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t t_o = tmem + 2u * kBN;
   auto t_s = [&](int j) { return tmem + static_cast<uint32_t>((j & 1) * kBN); };
-  auto t_o = [&](int j) { return tmem + 2u * kBN + static_cast<uint32_t>((j & 1) * kD); };
-  auto bar_s = [&](int j) { return smem_u32(&bars[j & 1]); };
-  auto bar_o = [&](int j) { return smem_u32(&bars[2 + (j & 1)]); };
 
-  // row of this thread
-  const int row = tid;
-  const int tok = tok0 + row / p.n_rep;
-  const int lim = p.causal ? (tok < nq ? sk - nq + tok : sk - 1) : sk - 1;
-  float acc[kD];
-#pragma unroll
-  for (int i = 0; i < kD; ++i) acc[i] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
-  bool failed = false;
-
-  // S(j) = Q K(j)^T into S buffer j&1 (issued by one thread)
-  auto issue_s = [&](int j) {
+  auto issue_s = [&](int j) {  // S(j) = Q K(j)^T
     tc::tc_fence_after();
     const uint32_t qa = smem_u32(qs), kb = smem_u32(ks + (j % kNBuf) * kKVBytes);
 #pragma unroll
@@ -163,8 +212,7 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
     }
     tc::mma_commit(bar_s(j));
   };
-  // O(j) = P(j) V(j) into O buffer j&1 (bf16: hi part then lo part)
-  auto issue_o = [&](int j) {
+  auto issue_o = [&](int j) {  // O += P(j) V(j)  (bf16: hi part then lo part)
     tc::tc_fence_after();
     const uint32_t vb = smem_u32(vs + (j % kNBuf) * kKVBytes);
     const int parts = kBf16 ? 2 : 1;
@@ -174,43 +222,42 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
       for (int kk = 0; kk < kBN / 16; ++kk) {
         const uint64_t ad = tc::smem_desc_sw128(pa + kk * 32, 16, 1024);
         const uint64_t bd = tc::smem_desc_sw128(vb + kk * 16 * 128, kBN * 128, 1024);
-        tc::mma_f16(t_o(j), ad, bd, id_o, (part > 0 || kk > 0) ? 1u : 0u);
+        tc::mma_f16(t_o, ad, bd, id_o, (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
       }
     }
     tc::mma_commit(bar_o(j));
   };
-  // acc = acc * alpha(j) + O(j)
-  auto fold = [&](int j, float alpha) {
-#pragma unroll
-    for (int c0 = 0; c0 < kD; c0 += 32) {
-      float o[32];
-      tc::tmem_ld32(t_o(j) + lane_base + c0, o);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) acc[c0 + i] = acc[c0 + i] * alpha + o[i];
-    }
-  };
 
-  if (n_tiles > 0) {
-    cp_async_wait<kNBuf - 2>();  // tile 0 resident
-    tc::fence_proxy_async_smem();
-    __syncthreads();
-    if (tid == 0) issue_s(0);
+  cp_async_wait<0>();  // Q (and, dense path, the prologue tiles) resident
+  tc::fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0 && n_tiles > 0) {
+    if (!tc::mbar_wait(bar_kv(0), 0)) *s_fail = 1;
+    else issue_s(0);
   }
 
-  for (int it = 0; it < n_tiles; ++it) {
-    // [A] tile it+1 resident -> S(it+1) can start while this tile's softmax runs
-    cp_async_wait<kNBuf - 3>();
-    tc::fence_proxy_async_smem();
-    tc::tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && it + 1 < n_tiles) issue_s(it + 1);
+  const int row = tid;
+  const int tok = tok0 + row / p.n_rep;
+  const int lim = p.causal ? (tok < nq ? sk - nq + tok : sk - 1) : sk - 1;
+  float m_ref = -INFINITY, l_run = 0.f;
+  bool failed = false;
 
-    const bool ok_s = tc::mbar_wait(bar_s(it), (it >> 1) & 1);
-    if (__syncthreads_or(!ok_s)) {
+  for (int it = 0; it < n_tiles; ++it) {
+    // [A] next tile's S on the tensor core while this tile's softmax runs
+    if (tid == 0 && it + 1 < n_tiles) {
+      if (!tc::mbar_wait(bar_kv(it + 1), ((it + 1) / kNBuf) & 1)) *s_fail = 1;
+      else issue_s(it + 1);
+    }
+    // [B] S(it) ready; O(it-1) accumulated (frees P, the K/V buffer of it-1, and O for a rescale)
+    bool ok = tc::mbar_wait(bar_s(it), (it >> 1) & 1);
+    if (it > 0) ok = ok && tc::mbar_wait(bar_o(it - 1), ((it - 1) >> 1) & 1);
+    if (__syncthreads_or(!ok || *s_fail)) {
       failed = true;
       break;
     }
     tc::tc_fence_after();
+    if (it + kNBuf - 1 < n_tiles) load_tile(it + kNBuf - 1);  // into the buffer tile it-1 used
+
     float s[kBN];
     tc::tmem_ld32(t_s(it) + lane_base, s);
     tc::tmem_ld32(t_s(it) + lane_base + 32, s + 32);
@@ -221,24 +268,25 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
       s[c] = (tbase + c <= lim) ? s[c] * p.scale_log2 : -INFINITY;
       mx = fmaxf(mx, s[c]);
     }
-    const float m_new = fmaxf(m_run, mx);
-    const float m_use = m_new == -INFINITY ? 0.f : m_new;
-    const float alpha = fast_exp2(m_run - m_use);
-    m_run = m_new;
-
-    // O(it-1) done: fold it, free its K/V buffer for tile it+3 and the P buffer
-    if (it > 0) {
-      const bool ok_o = tc::mbar_wait(bar_o(it - 1), ((it - 1) >> 1) & 1);
-      if (__syncthreads_or(!ok_o)) {
-        failed = true;
-        break;
-      }
-      tc::tc_fence_after();
-      fold(it - 1, alpha_prev);
+    // lazy reference max: move it (and rescale O, l) only when the row max grew by > threshold
+    const bool need = mx > m_ref + kRescaleThreshold;
+    float alpha = 1.f;
+    if (need) {
+      alpha = fast_exp2(m_ref - mx);  // 0 when m_ref = -inf
+      m_ref = mx;
+      l_run *= alpha;
     }
-    if (it + kNBuf - 1 < n_tiles) load_kv(it + kNBuf - 1, (it + kNBuf - 1) % kNBuf);
-    cp_async_commit();
-
+    if (it > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll
+      for (int c0 = 0; c0 < kD; c0 += 32) {
+        float o[32];
+        tc::tmem_ld32(t_o + lane_base + c0, o);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] *= alpha;
+        tmem_st32(t_o + lane_base + c0, o);
+      }
+    }
+    const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
     float sum = 0.f;
 #pragma unroll
     for (int c = 0; c < kBN; c += 8) {
@@ -253,40 +301,57 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
       *reinterpret_cast<uint4*>(ph + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
       if (kBf16) *reinterpret_cast<uint4*>(pl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
-    l_run = l_run * alpha + sum;
-    alpha_prev = alpha;
-    tc::fence_proxy_async_smem();  // P stores -> visible to the tensor core
+    l_run += sum;
+
+    if (it == n_tiles - 1 && kv_end < (it + 1) * kBN) {
+      // rows of the last page past kv_end hold whatever the pool page holds (P is 0
+      // there, but 0 * NaN is not): zero them in the V tile once it has landed
+      const bool okv = tc::mbar_wait(bar_kv(it), (it / kNBuf) & 1);
+      if (!okv) *s_fail = 1;
+      uint8_t* vb = vs + (it % kNBuf) * kKVBytes;
+      const int first = kv_end - it * kBN;
+      for (int e = tid; e < (kBN - first) * kDB * 8; e += 128) {
+        const int tt = first + e / (kDB * 8), rem = e % (kDB * 8);
+        *reinterpret_cast<uint4*>(vb + (rem >> 3) * (kBN * 128) + tt * 128 + (rem & 7) * 16) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    tc::fence_proxy_async_smem();  // P (and zeroed V rows) -> visible to the tensor core
     tc::tc_fence_before();
-    __syncthreads();  // [B]
+    // barrier + uniform failure vote (the flag is only ever read through the vote)
+    if (__syncthreads_or(*s_fail)) {
+      failed = true;
+      break;
+    }
     if (tid == 0) issue_o(it);
   }
   if (!failed && n_tiles > 0) {
     const int last = n_tiles - 1;
-    const bool ok_o = tc::mbar_wait(bar_o(last), (last >> 1) & 1);
-    if (__syncthreads_or(!ok_o)) {
-      failed = true;
-    } else {
-      tc::tc_fence_after();
-      fold(last, alpha_prev);
-    }
+    const bool ok = tc::mbar_wait(bar_o(last), (last >> 1) & 1);
+    if (__syncthreads_or(!ok)) failed = true;
   }
+  tc::tc_fence_after();
   cp_async_wait<0>();
 
-  // ---- epilogue ----
+  // ---- epilogue: O / l from TMEM ----
+  float acc[kD];
+  if (!failed && n_tiles > 0) {
+#pragma unroll
+    for (int c0 = 0; c0 < kD; c0 += 32) tc::tmem_ld32(t_o + lane_base + c0, acc + c0);
+  } else {
+#pragma unroll
+    for (int i = 0; i < kD; ++i) acc[i] = 0.f;
+  }
   if (tok < nq) {
-    const float inv = (l_run > 0.f && !failed) ? 1.f / l_run : 0.f;
+    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+    const float nan = __int_as_float(0x7fc00000);
     T* dst = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(q0 + tok) * p.Hq + hkv * p.n_rep + row % p.n_rep) * kD;
 #pragma unroll
     for (int c = 0; c < kD; c += 8) {
-      uint4 v;
-      if (failed) {
-        const float nan = __int_as_float(0x7fc00000);
-        v = make_uint4(pack2<T>(nan, nan), pack2<T>(nan, nan), pack2<T>(nan, nan), pack2<T>(nan, nan));
-      } else {
-        v = make_uint4(pack2<T>(acc[c] * inv, acc[c + 1] * inv), pack2<T>(acc[c + 2] * inv, acc[c + 3] * inv),
-                       pack2<T>(acc[c + 4] * inv, acc[c + 5] * inv), pack2<T>(acc[c + 6] * inv, acc[c + 7] * inv));
-      }
-      *reinterpret_cast<uint4*>(dst + c) = v;
+      float v[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = failed ? nan : acc[c + i] * inv;
+      *reinterpret_cast<uint4*>(dst + c) =
+          make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]), pack2<T>(v[6], v[7]));
     }
   }
   tc::tc_fence_before();
@@ -297,15 +362,60 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(PrefillTcParams p) {
   }
 }
 
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 4-D view of one pool layer: (head_dim, kv_head, token-in-page, page); one
+// box = 64 elements of head_dim x 1 head x 16 tokens of one page, 128-B swizzle.
+bool make_page_map(CUtensorMap* map, const void* base, int Hkv, int64_t page_stride, bool bf16) {
+  EncodeTiledFn enc = encode_fn();
+  if (enc == nullptr) return false;
+  const cuuint64_t dims[4] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(Hkv), 16, 1u << 24};
+  const cuuint64_t strides[3] = {static_cast<cuuint64_t>(kD) * 2, static_cast<cuuint64_t>(Hkv) * kD * 2,
+                                 static_cast<cuuint64_t>(page_stride) * 2};
+  const cuuint32_t box[4] = {64, 1, 16, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(base),
+             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace
 
 // Launches the tcgen05 kernel; returns BPKV_ERR_UNSUPPORTED when the shape is
 // not one it handles (head_dim 128, bf16/fp16, n_rep dividing 128).
 int prefill_tc_launch(PrefillTcParams& p, int head_dim, int dtype, int max_seqlen_q, bool paged, cudaStream_t st) {
   if (head_dim != kD || (dtype != BPKV_BF16 && dtype != BPKV_F16) || kBM % p.n_rep != 0) return BPKV_ERR_UNSUPPORTED;
+  if (paged && (p.page_stride * 2) % 16 != 0) return BPKV_ERR_UNSUPPORTED;
   const int TQ = kBM / p.n_rep;
   p.tiles_per_req = (max_seqlen_q + TQ - 1) / TQ;
   if (p.tiles_per_req == 0 || p.B == 0) return BPKV_OK;
+  TcKernelArgs args;
+  memset(&args, 0, sizeof(args));
+  args.p = p;
+  if (paged) {
+    if (!make_page_map(&args.tmap_k, p.k, p.Hkv, p.page_stride, dtype == BPKV_BF16) ||
+        !make_page_map(&args.tmap_v, p.v, p.Hkv, p.page_stride, dtype == BPKV_BF16)) {
+      set_error("prefill_tc_launch:tensor_map_encode_failed");
+      return BPKV_ERR_CUDA;
+    }
+  }
   dim3 grid(p.B * p.tiles_per_req, p.Hkv);
   static bool raised[4][64] = {};
   int dev = 0;
@@ -321,7 +431,7 @@ int prefill_tc_launch(PrefillTcParams& p, int head_dim, int dtype, int max_seqle
       }                                                                                                    \
       raised[variant][dev] = true;                                                                         \
     }                                                                                                      \
-    kern<<<grid, 128, kSmemBytes, st>>>(p);                                                                \
+    kern<<<grid, 128, kSmemBytes, st>>>(args);                                                             \
   } while (0)
   if (dtype == BPKV_BF16) {
     if (paged) BPKV_TC_LAUNCH(__nv_bfloat16, true); else BPKV_TC_LAUNCH(__nv_bfloat16, false);

@@ -130,6 +130,19 @@ def stream_ptr(device: torch.device | None = None) -> int:
 _ws_cache: dict = {}
 
 
+def workspace_for(nbytes: int, device: torch.device, stream, tag: str) -> torch.Tensor:
+    """Like ``workspace`` for a stream object the caller already holds.  The
+    library calls run with that stream current on the tensor's device (the
+    caller's device context), so no device switch is needed here."""
+    key = (device.index, stream.cuda_stream, tag)
+    buf = _ws_cache.get(key)
+    if buf is None or buf.numel() < nbytes:
+        with torch.cuda.device(device):
+            buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+        _ws_cache[key] = buf
+    return buf
+
+
 def workspace(nbytes: int, device: torch.device, tag: str = "default") -> torch.Tensor:
     """A per-(device, stream, tag) byte buffer reused across calls.
 

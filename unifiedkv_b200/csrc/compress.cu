@@ -24,6 +24,20 @@
 #include "common.cuh"
 
 namespace bpkv {
+
+struct ScoreTcParams {
+  const void* k;
+  const void* q;
+  int Hkv, n_rep, W, Wp, Lm, Tm, sink, n_chunks;
+  int64_t k_sh, k_st, q_sh, q_st;
+  float scale_log2;
+  float2* ml_part;
+  const float2* ml;
+  float* headmax;
+};
+// tcgen05 scoring passes (compress_tc.cu); BPKV_ERR_UNSUPPORTED if the shape does not fit.
+int score_tc_pass(ScoreTcParams& p, int head_dim, int dtype, int pass, cudaStream_t st);
+
 namespace {
 
 constexpr int kTileTok = 64;    // tokens per mma tile
@@ -427,6 +441,37 @@ ScoreWs score_ws(int Hq, int W, int L, int sink, int obs) {
 
 template <typename T, int D>
 int launch_score(ScoreParams& p, float* out, int N, int smooth, cudaStream_t st) {
+  if constexpr (D == 128) {
+    ScoreTcParams t{};
+    t.k = p.k;
+    t.q = p.q;
+    t.Hkv = p.Hkv;
+    t.n_rep = p.n_rep;
+    t.W = p.W;
+    t.Wp = p.Wp;
+    t.Lm = p.Lm;
+    t.Tm = p.Tm;
+    t.sink = p.sink;
+    t.k_sh = p.k_sh;
+    t.k_st = p.k_st;
+    t.q_sh = p.q_sh;
+    t.q_st = p.q_st;
+    t.scale_log2 = p.scale_log2;
+    t.ml_part = p.ml_part;
+    t.ml = p.ml;
+    t.headmax = p.headmax;
+    const int dt = std::is_same<T, __nv_bfloat16>::value ? BPKV_BF16 : BPKV_F16;
+    int rc = score_tc_pass(t, D, dt, 1, st);
+    if (rc != BPKV_ERR_UNSUPPORTED) {
+      if (rc != BPKV_OK) return rc;
+      const int nrows = p.Hq * p.Wp;
+      stats_reduce_kernel<<<(nrows * 32 + 255) / 256, 256, 0, st>>>(p.ml_part, p.ml, nrows, t.n_chunks);
+      rc = score_tc_pass(t, D, dt, 2, st);
+      if (rc != BPKV_OK) return rc;
+      block_reduce_kernel<<<(N + kBlkPerCta - 1) / kBlkPerCta, 256, 0, st>>>(p.headmax, out, p.Hkv, p.Tm, N, smooth);
+      BPKV_RETURN_LAUNCH("block_score_launch");
+    }
+  }
   const int rows = p.n_rep * p.Wp;
   const size_t smem = static_cast<size_t>(rows) * D * 2 + 2 * kTileTok * D * 2 +
                       sizeof(float) * max(rows / 16 * kTileTok, 2 * rows);

@@ -486,36 +486,40 @@ __device__ void lse_merge_row(const float* part_o, const float* part_lse, int64_
   if (lse_out != nullptr && tid == 0) *lse_out = M + logf(W);
 }
 
-// Combine of split requests.  CTA (b, head group of kCombineHeads) gathers the
-// list of CTAs that own pages of request b (ranges can be empty when T < G;
-// those wrote nothing and are skipped), turns the per-slot lse into normalised
-// weights once in shared memory, then forms out = sum_i w_i o_i with coalesced
-// reads.  Requests without pages get NaN rows (the reference's 0/0); requests
-// owned by a single CTA were finished by the decode kernel and are skipped.
-constexpr int kCombineHeads = 8;
+// Combine of split requests.  CTA (b, q-head), 8 warps.  The CTAs that own
+// pages of request b are c_lo..c_hi; when every CTA range is non-empty
+// (T >= G) their slots are simply c + b, otherwise (few pages) the empty
+// ranges are skipped with a short serial scan.  Weights exp(lse_i - M) are
+// formed once in shared memory; warp w accumulates parts w, w+8, ... over all
+// head_dim columns (coalesced rows of the partial buffer), then the 8 warp
+// sums are added in a fixed order.  Requests without pages get NaN rows (the
+// reference's 0/0); requests owned by a single CTA were finished by the decode
+// kernel.
 constexpr int kMaxSlotsPerReq = 1024;  // >= 2 * SM count
+constexpr int kCombWarps = 8;
 
 template <typename T>
-__global__ void __launch_bounds__(256) page16_decode_combine_kernel(DecodeParams p, int G) {
+__global__ void __launch_bounds__(kCombWarps * 32) page16_decode_combine_kernel(DecodeParams p, int G) {
   __shared__ int s_slot[kMaxSlotsPerReq];
-  __shared__ float s_w[kCombineHeads][kMaxSlotsPerReq];
-  __shared__ float s_lse[kCombineHeads];
+  __shared__ float s_w[kMaxSlotsPerReq];
+  __shared__ float s_red[kCombWarps];
+  __shared__ float s_acc[kCombWarps][256];
   __shared__ int s_n;
-  const int b = blockIdx.x;
-  const int h0 = blockIdx.y * kCombineHeads;
-  const int nh = min(kCombineHeads, p.Hq - h0);
+  const int b = blockIdx.x, hq = blockIdx.y;
   const int64_t T_ = p.g_prefix[p.B];
   const int64_t first = p.g_prefix[b], last = p.g_prefix[b + 1];
   const int D = p.D;
-  T* ob = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.Hq + h0) * D;
+  T* ob = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.Hq + hq) * D;
+  float* lse_dst = p.lse_out ? p.lse_out + static_cast<int64_t>(b) * p.Hq + hq : nullptr;
   if (last == first) {
-    for (int i = threadIdx.x; i < nh * D; i += blockDim.x) ob[i] = Elem<T>::from_f(__int_as_float(0x7fc00000));
-    if (p.lse_out != nullptr && threadIdx.x < nh) p.lse_out[static_cast<int64_t>(b) * p.Hq + h0 + threadIdx.x] = -INFINITY;
+    for (int d = threadIdx.x; d < D; d += blockDim.x) ob[d] = Elem<T>::from_f(__int_as_float(0x7fc00000));
+    if (lse_dst != nullptr && threadIdx.x == 0) *lse_dst = -INFINITY;
     return;
   }
   const int c_lo = owner_of_page(first, T_, G), c_hi = owner_of_page(last - 1, T_, G);
   if (c_lo == c_hi) return;
-  if (threadIdx.x == 0) {
+  const bool dense = T_ >= G;  // every CTA owns >= 1 page
+  if (!dense && threadIdx.x == 0) {
     int n = 0;
     int64_t start = range_start(c_lo, T_, G);
     for (int c = c_lo; c <= c_hi && n < kMaxSlotsPerReq; ++c) {
@@ -526,34 +530,55 @@ __global__ void __launch_bounds__(256) page16_decode_combine_kernel(DecodeParams
     s_n = n;
   }
   __syncthreads();
-  const int n = s_n;
-  // one warp per head: max, sum, normalised weights
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int h = warp; h < nh; h += blockDim.x >> 5) {
-    const int hq = h0 + h;
-    float M = -INFINITY;
-    for (int i = lane; i < n; i += 32) M = fmaxf(M, p.part_lse[static_cast<int64_t>(s_slot[i]) * p.Hq + hq]);
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    float W = 0.f;
-    for (int i = lane; i < n; i += 32) {
-      const float w = expf(p.part_lse[static_cast<int64_t>(s_slot[i]) * p.Hq + hq] - M);
-      s_w[h][i] = w;
-      W += w;
+  const int n = dense ? min(c_hi - c_lo + 1, kMaxSlotsPerReq) : s_n;
+  auto slot = [&](int i) { return dense ? (c_lo + i + b) : s_slot[i]; };
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float M = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) M = fmaxf(M, p.part_lse[static_cast<int64_t>(slot(i)) * p.Hq + hq]);
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if (lane == 0) s_red[warp] = M;
+  __syncthreads();
+  M = s_red[0];
+  for (int w = 1; w < kCombWarps; ++w) M = fmaxf(M, s_red[w]);
+  __syncthreads();
+  float W = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float w = expf(p.part_lse[static_cast<int64_t>(slot(i)) * p.Hq + hq] - M);
+    s_w[i] = w;
+    W += w;
+  }
+  for (int o = 16; o > 0; o >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o);
+  if (lane == 0) s_red[warp] = W;
+  __syncthreads();
+  W = 0.f;
+  for (int w = 0; w < kCombWarps; ++w) W += s_red[w];
+  // warp-strided accumulation over parts; lanes cover head_dim (<= 256)
+  float acc[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+#pragma unroll 4
+  for (int i = warp; i < n; i += kCombWarps) {
+    const float w = s_w[i];
+    const float* po = p.part_o + (static_cast<int64_t>(slot(i)) * p.Hq + hq) * D;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int d = lane + 32 * k;
+      if (d < D) acc[k] += w * po[d];
     }
-    for (int o = 16; o > 0; o >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o);
-    const float inv = 1.f / W;
-    for (int i = lane; i < n; i += 32) s_w[h][i] *= inv;
-    if (lane == 0) s_lse[h] = M + logf(W);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int d = lane + 32 * k;
+    if (d < D) s_acc[warp][d] = acc[k];
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < nh * D; e += blockDim.x) {
-    const int h = e / D, d = e % D;
-    const float* po = p.part_o + static_cast<int64_t>(h0 + h) * D + d;
+  const float inv = 1.f / W;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float a = 0.f;
-    for (int i = 0; i < n; ++i) a += s_w[h][i] * po[static_cast<int64_t>(s_slot[i]) * p.Hq * D];
-    ob[static_cast<int64_t>(h) * D + d] = Elem<T>::from_f(a);
+    for (int w = 0; w < kCombWarps; ++w) a += s_acc[w][d];
+    ob[d] = Elem<T>::from_f(a * inv);
   }
-  if (p.lse_out != nullptr && threadIdx.x < nh) p.lse_out[static_cast<int64_t>(b) * p.Hq + h0 + threadIdx.x] = s_lse[threadIdx.x];
+  if (lse_dst != nullptr && threadIdx.x == 0) *lse_dst = M + logf(W);
 }
 
 template <typename T>
@@ -634,7 +659,7 @@ int launch_mma(DecodeParams& p, cudaStream_t st) {
     return BPKV_ERR_CUDA;
   }
   kern<<<dim3(G, groups), NW * 32, smem, st>>>(p);
-  page16_decode_combine_kernel<T><<<dim3(p.B, (p.Hq + kCombineHeads - 1) / kCombineHeads), 256, 0, st>>>(p, G);
+  page16_decode_combine_kernel<T><<<dim3(p.B, p.Hq), kCombWarps * 32, 0, st>>>(p, G);
   BPKV_RETURN_LAUNCH("page16_native_launch");
 }
 
@@ -650,7 +675,7 @@ int launch_generic(DecodeParams& p, cudaStream_t st) {
     return BPKV_ERR_CUDA;
   }
   kern<<<G, NW * 32, smem, st>>>(p);
-  page16_decode_combine_kernel<T><<<dim3(p.B, (p.Hq + kCombineHeads - 1) / kCombineHeads), 256, 0, st>>>(p, G);
+  page16_decode_combine_kernel<T><<<dim3(p.B, p.Hq), kCombWarps * 32, 0, st>>>(p, G);
   BPKV_RETURN_LAUNCH("page16_native_launch");
 }
 

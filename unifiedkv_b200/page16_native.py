@@ -21,7 +21,7 @@ HAS_PAGE16_NATIVE = HAS_TRITON
 def _check_shapes(q, k_cache, v_cache, block_table, cache_seqlens):
     """Argument validation with the reference's exact error tokens
     (core/page16_native.py:100-124)."""
-    if not _lib.available():
+    if not HAS_TRITON:
         raise RuntimeError("page16_native_unavailable:native_library_not_loaded")
     if q.dim() != 3:
         raise RuntimeError(f"page16_native_shape_unsupported:q_dim_{q.dim()}")
@@ -103,17 +103,21 @@ def page16_decode_attention(
         if lse_out.dtype != torch.float32 or lse_out.numel() != batch * num_q_heads or not lse_out.is_contiguous():
             raise RuntimeError("page16_native_shape_unsupported:lse_out")
     dev = q.device
+    if dev.index != torch.cuda.current_device():  # the library launches on the current device
+        with torch.cuda.device(dev):
+            return page16_decode_attention(q, k_cache, v_cache, block_table, cache_seqlens,
+                                           softmax_scale=softmax_scale, n_rep=n_rep, lse_out=lse_out)
     L = _lib.lib()
-    with torch.cuda.device(dev):
-        code = _lib.dtype_code(q.dtype)
-        nbytes = L.bpkv_page16_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, code)
-        ws = _lib.workspace(nbytes, dev, "page16")
-        rc = L.bpkv_page16_decode(
-            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
-            cache_seqlens.data_ptr(), out.data_ptr(), _lib.ptr(lse_out),
-            batch, num_q_heads, num_kv_heads, head_dim, int(block_table.shape[1]),
-            q.stride(0), q.stride(1), k_cache.stride(0), block_table.stride(0),
-            float(softmax_scale), code, ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+    code = _lib.dtype_code(q.dtype)
+    stream = torch.cuda.current_stream(dev)
+    ws = _lib.workspace_for(L.bpkv_page16_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, code),
+                            dev, stream, "page16")
+    rc = L.bpkv_page16_decode(
+        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
+        cache_seqlens.data_ptr(), out.data_ptr(), _lib.ptr(lse_out),
+        batch, num_q_heads, num_kv_heads, head_dim, int(block_table.shape[1]),
+        q.stride(0), q.stride(1), k_cache.stride(0), block_table.stride(0),
+        float(softmax_scale), code, ws.data_ptr(), ws.numel(), stream.cuda_stream)
     _lib.check(rc, "page16_native")
     return out
 

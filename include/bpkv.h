@@ -173,7 +173,7 @@ BPKV_API int bpkv_block_score(const void* k, const void* q_obs, float* block_sco
  * torch.topk + sorted(set(...)) (core/scheduler.py:615-616); ties are broken by
  * the LOWEST block index (torch leaves tie order unspecified).
  * scores: fp32 [n]; selected: int32 [k] written in ascending index order.
- * n <= 65536.  NaN scores rank above every number (as torch.topk).
+ * n <= 49152.  NaN scores rank above every number (as torch.topk).
  * ------------------------------------------------------------------------ */
 BPKV_API int bpkv_topk_select(const float* scores, int n, int k, int32_t* selected, void* stream);
 

@@ -47,7 +47,7 @@ def test_block_scores(cuda, dtype, spec):
     assert np.allclose(got, ref, rtol=1e-4, atol=1e-7), np.max(np.abs(got - ref) / ref)
 
 
-@pytest.mark.parametrize("n,k", [(1, 1), (5, 2), (173, 40), (2044, 511), (3000, 1), (16384, 4096), (100, 0)])
+@pytest.mark.parametrize("n,k", [(1, 1), (5, 2), (173, 40), (2044, 511), (3000, 1), (16384, 4096), (49152, 30000), (100, 0)])
 def test_topk_bit_exact_with_ties(cuda, n, k):
     from unifiedkv_b200.compress import topk_blocks
     rng = np.random.default_rng(n + k)

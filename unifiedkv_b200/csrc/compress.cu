@@ -301,62 +301,108 @@ __device__ __forceinline__ uint32_t desc_key(float f) {
   return ~ord;
 }
 
-__global__ void __launch_bounds__(1024) topk_select_kernel(const float* scores, int n, int k, int32_t* selected) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  int npow = 1;
-  while (npow < n) npow <<= 1;
-  uint64_t* key = reinterpret_cast<uint64_t*>(smem);
-  int* flag = reinterpret_cast<int*>(key + npow);
-  __shared__ int wsum[32];
-  const int tid = threadIdx.x, nt = blockDim.x;
-  for (int i = tid; i < npow; i += nt) {
-    key[i] = (i < n) ? ((static_cast<uint64_t>(desc_key(scores[i])) << 32) | static_cast<uint32_t>(i))
-                     : ~0ull;
-  }
-  for (int i = tid; i < n; i += nt) flag[i] = 0;
-  __syncthreads();
-  for (int size = 2; size <= npow; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < npow / 2; i += nt) {
-        const int lo = 2 * i - (i & (stride - 1));
-        const int hi = lo + stride;
-        const bool asc = (lo & size) == 0;
-        const uint64_t a = key[lo], b = key[hi];
-        if ((a > b) == asc) {
-          key[lo] = b;
-          key[hi] = a;
-        }
-      }
-      __syncthreads();
-    }
-  }
-  for (int i = tid; i < k; i += nt) flag[static_cast<uint32_t>(key[i])] = 1;
-  __syncthreads();
-  // ordered compaction of flagged indices
-  const int per = (n + nt - 1) / nt;
-  const int beg = tid * per, end = min(beg + per, n);
-  int local = 0;
-  for (int i = beg; i < end; ++i) local += flag[i];
-  const int lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
+// Exclusive block scan of per-thread counts (threads own contiguous index ranges).
+__device__ int block_exclusive_scan(int local, int* wsum) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   int incl = local;
   for (int o = 1; o < 32; o <<= 1) {
-    int y = __shfl_up_sync(0xffffffffu, incl, o);
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
     if (lane >= o) incl += y;
   }
+  __syncthreads();
   if (lane == 31) wsum[warp] = incl;
   __syncthreads();
   if (warp == 0) {
-    int w = lane < nw ? wsum[lane] : 0, wi = w;
+    const int w = lane < nw ? wsum[lane] : 0;
+    int wi = w;
     for (int o = 1; o < 32; o <<= 1) {
-      int y = __shfl_up_sync(0xffffffffu, wi, o);
+      const int y = __shfl_up_sync(0xffffffffu, wi, o);
       if (lane >= o) wi += y;
     }
     wsum[lane] = wi - w;
   }
   __syncthreads();
-  int pos = wsum[warp] + incl - local;
-  for (int i = beg; i < end; ++i)
-    if (flag[i]) selected[pos++] = i;
+  return wsum[warp] + incl - local;
+}
+
+// Top-k by radix select on 32-bit order keys (smaller key = higher score):
+// four 8-bit passes find the exact k-th smallest key T and how many keys equal
+// to T are still needed; the selection is every key < T plus the first of the
+// keys == T in index order (ties -> lowest index), written in ascending index
+// order by an ordered compaction.
+__global__ void __launch_bounds__(1024) topk_select_kernel(const float* scores, int n, int k, int32_t* selected) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint32_t* key = reinterpret_cast<uint32_t*>(smem);
+  __shared__ int hist[256];
+  __shared__ int wsum[32];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_need;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  for (int i = tid; i < n; i += nt) key[i] = desc_key(scores[i]);
+  if (tid == 0) {
+    s_prefix = 0;
+    s_need = k;
+  }
+  uint32_t mask = 0;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int b = tid; b < 256; b += nt) hist[b] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix;
+    for (int i = tid; i < n; i += nt) {
+      const uint32_t kv = key[i];
+      if ((kv & mask) == prefix) atomicAdd(&hist[(kv >> shift) & 255u], 1);
+    }
+    __syncthreads();
+    if (tid < 32) {  // warp 0: bin where the cumulative count reaches s_need
+      const int need = s_need;
+      int c[8], run = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        c[j] = hist[tid * 8 + j];
+        run += c[j];
+      }
+      int incl = run;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (tid >= o) incl += y;
+      }
+      int before = incl - run;
+      const bool mine = before < need && incl >= need;
+      if (mine) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (before + c[j] >= need) {
+            s_prefix = prefix | (static_cast<uint32_t>(tid * 8 + j) << shift);
+            s_need = need - before;
+            break;
+          }
+          before += c[j];
+        }
+      }
+    }
+    mask |= 255u << shift;
+    __syncthreads();
+  }
+  const uint32_t T = s_prefix;
+  const int need_eq = s_need;
+  const int per = (n + nt - 1) / nt;
+  const int beg = min(tid * per, n), end = min(beg + per, n);
+  int eq_local = 0;
+  for (int i = beg; i < end; ++i) eq_local += key[i] == T;
+  int eq_rank = block_exclusive_scan(eq_local, wsum);
+  int sel_local = 0;
+  for (int i = beg; i < end; ++i) {
+    const uint32_t kv = key[i];
+    const bool take = kv < T || (kv == T && eq_rank++ < need_eq);
+    sel_local += take;
+  }
+  int pos = block_exclusive_scan(sel_local, wsum);
+  eq_rank = block_exclusive_scan(eq_local, wsum);
+  for (int i = beg; i < end; ++i) {
+    const uint32_t kv = key[i];
+    const bool take = kv < T || (kv == T && eq_rank++ < need_eq);
+    if (take) selected[pos++] = i;
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -573,18 +619,16 @@ extern "C" BPKV_API int bpkv_block_score(const void* k, const void* q_obs, float
 extern "C" BPKV_API int bpkv_topk_select(const float* scores, int n, int k, int32_t* selected, void* stream) {
   clear_error();
   BPKV_CHECK_ARG(n >= 0 && k >= 0 && k <= n, "selected_writeback_topk_shape:n_%d_k_%d", n, k);
-  BPKV_CHECK_ARG(n <= 16384, "selected_writeback_topk_shape:n_%d_exceeds_16384", n);
+  BPKV_CHECK_ARG(n <= 49152, "selected_writeback_topk_shape:n_%d_exceeds_49152", n);
   if (k == 0) return BPKV_OK;
   BPKV_CHECK_ARG(scores && selected, "selected_writeback_topk_shape:null_pointer");
-  int npow = 1;
-  while (npow < n) npow <<= 1;
-  const size_t smem = sizeof(uint64_t) * npow + sizeof(int) * n;
+  const size_t smem = sizeof(uint32_t) * n;
   static bool raised[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (smem > 48 * 1024 && dev < 64 && !raised[dev]) {
     cudaFuncSetAttribute(topk_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(sizeof(uint64_t) * 16384 + sizeof(int) * 16384));
+                         static_cast<int>(sizeof(uint32_t) * 49152));
     raised[dev] = true;
   }
   topk_select_kernel<<<1, 1024, smem, static_cast<cudaStream_t>(stream)>>>(scores, n, k, selected);

@@ -15,7 +15,7 @@ from pathlib import Path
 import torch
 
 _PKG = Path(__file__).resolve().parent
-LIB_PATH = _PKG / "lib" / "libbpkv.so"
+LIB_PATH = _PKG / "lib" / ("libbpkv_trace.so" if os.environ.get("BPKV_TRACE") == "1" else "libbpkv.so")
 
 BPKV_OK, BPKV_ERR_SHAPE, BPKV_ERR_UNSUPPORTED, BPKV_ERR_CUDA, BPKV_ERR_WORKSPACE = 0, 1, 2, 3, 4
 BPKV_F32, BPKV_F16, BPKV_BF16 = 0, 1, 2

@@ -14,7 +14,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIBDIR = PKG / "lib"
-LIB = LIBDIR / "libbpkv.so"
+LIB = LIBDIR / ("libbpkv_trace.so" if os.environ.get("BPKV_TRACE") == "1" else "libbpkv.so")
 INCLUDE = PKG.parent / "include"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -49,7 +49,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     if not force and not _stale():
         return LIB
     LIBDIR.mkdir(parents=True, exist_ok=True)
-    objdir = LIBDIR / "obj"
+    objdir = LIBDIR / ("obj_trace" if os.environ.get("BPKV_TRACE") == "1" else "obj")
     objdir.mkdir(exist_ok=True)
     nvcc = _nvcc()
     objs = []
@@ -57,6 +57,8 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
     for src in sources():
         obj = objdir / (src.stem + ".o")
         cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
+        if os.environ.get("BPKV_TRACE") == "1":  # debug instrumentation build (separate library)
+            cmd += ["-DBPKV_TRACE"]
         if ptxas_verbose:
             cmd += ["-Xptxas", "-v"]
         if verbose:

@@ -43,15 +43,30 @@ struct PrefillTcParams {
   float scale_log2;
 };
 
+#ifdef BPKV_TRACE
+// Debug builds only (-DBPKV_TRACE): per-phase clock64 totals of CTA (0,0).
+__device__ unsigned long long g_prefill_trace[16];
+#define BPKV_T0() const long long _t0 = clock64()
+#define BPKV_TADD(slot) atomicAdd(&g_prefill_trace[slot], static_cast<unsigned long long>(clock64() - _t0))
+#define BPKV_TRACING (blockIdx.x == 0 && blockIdx.y == 0)
+#endif
+
 namespace {
 
 constexpr int kD = 128, kBM = 128, kBN = 64, kDB = kD / 64;
 constexpr int kQBytes = kDB * kBM * 128;       // 32 KB
 constexpr int kKVBytes = kDB * kBN * 128;      // 16 KB per K or V tile
 constexpr int kPBytes = kBM * 128;             // 16 KB (64 tokens per row)
-constexpr int kNBuf = 4;                       // K/V ring depth
-constexpr int kMaxPagesSmem = 4096;            // block-table entries staged in shared memory
-constexpr int kSmemBytes = kQBytes + 2 * kNBuf * kKVBytes + 2 * kPBytes + 1024 /*align*/ + 128 + 4 * kMaxPagesSmem;
+constexpr int kNK = 4;                         // K ring depth (K(j) is free once S(j) was consumed)
+constexpr int kNV = 3;                         // V ring depth (V(j) is free once PV(j) completed)
+constexpr int kPBufBytes = 2 * kPBytes;        // one P buffer: hi + lo parts
+constexpr int kSoftmaxWarps = 8;               // warps 0-7: softmax (two per row group)
+constexpr int kLoadWarp = kSoftmaxWarps;       // warp 8: TMA / cp.async loads
+constexpr int kMmaWarp = kSoftmaxWarps + 1;    // warp 9: tcgen05.mma issue
+constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
+constexpr int kMaxPagesSmem = 2048;            // block-table entries staged in shared memory
+constexpr int kSmemBytes = kQBytes + (kNK + kNV) * kKVBytes + 2 * kPBufBytes + 1024 /*align*/ + 256 + 4 * kMaxPagesSmem +
+                            4 * 2 * 2 * kBM /*row-max exchange*/ + 4 * 2 * kBM /*row sums*/;
 constexpr uint32_t kTmemCols = 256;            // S0 [0,64) S1 [64,128) O [128,256)
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 256 between rescales
 
@@ -93,19 +108,21 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
 }
 
 template <typename T, bool PAGED>
-__global__ void __launch_bounds__(128, 1) prefill_tc_kernel(const __grid_constant__ TcKernelArgs args) {
+__global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ TcKernelArgs args) {
   const PrefillTcParams& p = args.p;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* qs = smem;
-  uint8_t* ks = qs + kQBytes;            // kNBuf buffers
-  uint8_t* vs = ks + kNBuf * kKVBytes;   // kNBuf buffers
-  uint8_t* ph = vs + kNBuf * kKVBytes;
-  uint8_t* pl = ph + kPBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(pl + kPBytes);  // kv[4], s[2], o[2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint8_t* ks = qs + kQBytes;            // kNK buffers
+  uint8_t* vs = ks + kNK * kKVBytes;     // kNV buffers
+  uint8_t* ps = vs + kNV * kKVBytes;     // 2 P buffers, each hi + lo
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + 2 * kPBufBytes);
+  // bars: k_full[kNK], v_full[kNV], s_full[2], p_full[2], o_done[2], k_free[kNK], v_free[kNV]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * (kNK + kNV) + 6);
   int* s_fail = reinterpret_cast<int*>(tmem_slot + 1);
-  int* s_pages = reinterpret_cast<int*>(bars + 16);  // this request's block-table row (paged)
+  int* s_pages = reinterpret_cast<int*>(bars + 32);
+  float* s_mx = reinterpret_cast<float*>(s_pages + kMaxPagesSmem);  // [2 buffers][2 halves][kBM]
+  float* s_l = s_mx + 4 * kBM;                                         // [2 halves][kBM]
 
   const int b = blockIdx.x / p.tiles_per_req;
   const int qt = blockIdx.x % p.tiles_per_req;
@@ -116,27 +133,39 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(const __grid_constan
   const int tok0 = qt * TQ;
   if (tok0 >= nq) return;  // uniform across the CTA: before any barrier or TMEM use
   const int sk = PAGED ? p.seqlens_k[b] : nq;
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const T* qg = reinterpret_cast<const T*>(p.q);
   const T* kg = reinterpret_cast<const T*>(p.k);
   const T* vg = reinterpret_cast<const T*>(p.v);
-  auto bar_kv = [&](int t) { return smem_u32(&bars[t % kNBuf]); };
-  auto bar_s = [&](int j) { return smem_u32(&bars[4 + (j & 1)]); };
-  auto bar_o = [&](int j) { return smem_u32(&bars[6 + (j & 1)]); };
+  auto k_full = [&](int t) { return smem_u32(&bars[t % kNK]); };
+  auto v_full = [&](int t) { return smem_u32(&bars[kNK + t % kNV]); };
+  auto s_full = [&](int j) { return smem_u32(&bars[kNK + kNV + (j & 1)]); };
+  auto p_full = [&](int j) { return smem_u32(&bars[kNK + kNV + 2 + (j & 1)]); };
+  auto o_done = [&](int j) { return smem_u32(&bars[kNK + kNV + 4 + (j & 1)]); };
+  auto k_free = [&](int t) { return smem_u32(&bars[kNK + kNV + 6 + t % kNK]); };
+  auto v_free = [&](int t) { return smem_u32(&bars[2 * kNK + kNV + 6 + t % kNV]); };
+  auto p_hi = [&](int j) { return ps + (j & 1) * kPBufBytes; };
+  auto p_lo = [&](int j) { return ps + (j & 1) * kPBufBytes + kPBytes; };
 
   if (warp == 0) {
     tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < 4; ++i) tc::mbar_init(smem_u32(&bars[i]), PAGED ? 1u : 128u);
-    for (int i = 4; i < 8; ++i) tc::mbar_init(smem_u32(&bars[i]), 1u);
+    for (int i = 0; i < kNK + kNV; ++i) tc::mbar_init(smem_u32(&bars[i]), PAGED ? 1u : 32u);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(s_full(i), 1u);
+      tc::mbar_init(p_full(i), 32u * kSoftmaxWarps);
+      tc::mbar_init(o_done(i), 1u);
+    }
+    for (int i = 0; i < kNK; ++i) tc::mbar_init(k_free(i), 1u);
+    for (int i = 0; i < kNV; ++i) tc::mbar_init(v_free(i), 1u);
     *s_fail = 0;
     tc::fence_mbar_init();
   }
 
-  // ---- Q tile: row m = (token tok0 + m / n_rep, head m % n_rep) ----
-  for (int ci = tid; ci < kBM * (kD / 8); ci += 128) {
+  // ---- Q tile: row m = (token tok0 + m / n_rep, head m % n_rep), all threads ----
+  for (int ci = tid; ci < kBM * (kD / 8); ci += kThreads) {
     const int m = ci / (kD / 8), ch = ci % (kD / 8);
     const int tok = tok0 + m / p.n_rep, r = m % p.n_rep;
     const bool ok = tok < nq;
@@ -147,213 +176,281 @@ __global__ void __launch_bounds__(128, 1) prefill_tc_kernel(const __grid_constan
   const int last_tok = min(tok0 + TQ, nq) - 1;
   const int kv_end = p.causal ? min(sk, sk - nq + last_tok + 1) : sk;
   const int n_tiles = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
-
   if constexpr (PAGED) {
     const int np = min((kv_end + kPage - 1) / kPage, kMaxPagesSmem);
-    for (int i = tid; i < np; i += 128) s_pages[i] = __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + i);
+    for (int i = tid; i < np; i += kThreads) s_pages[i] = __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + i);
   }
+  cp_async_wait<0>();
+  tc::fence_proxy_async_smem();
   tc::tc_fence_before();
-  __syncthreads();  // barriers initialised, TMEM address published, block-table row staged
+  __syncthreads();  // Q resident, barriers initialised, TMEM address published, block table staged
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
-  // K/V tile t -> ring buffer t % kNBuf
-  auto load_tile = [&](int t) {
-    const int buf = t % kNBuf;
-    if constexpr (PAGED) {
-      if (tid == 0) {
-        const int pg0 = t * (kBN / kPage);
-        int npg = 0;
-        for (int pg = 0; pg < kBN / kPage; ++pg)
-          if ((pg0 + pg) * kPage < kv_end) ++npg;
-        mbar_expect_tx(bar_kv(t), static_cast<uint32_t>(npg * 2 * kDB * kPage * 128));
-        for (int pg = 0; pg < npg; ++pg) {
-          const int idx = pg0 + pg;
-          const int page = idx < kMaxPagesSmem ? s_pages[idx] : __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + idx);
-#pragma unroll
-          for (int db = 0; db < kDB; ++db) {
-            const uint32_t off = buf * kKVBytes + db * (kBN * 128) + pg * kPage * 128;
-            tma_load_4d(smem_u32(ks + off), &args.tmap_k, db * 64, hkv, 0, page, bar_kv(t));
-            tma_load_4d(smem_u32(vs + off), &args.tmap_v, db * 64, hkv, 0, page, bar_kv(t));
-          }
-        }
-      }
-    } else {
-      for (int ci = tid; ci < kBN * (kD / 8); ci += 128) {
-        const int tt = ci / (kD / 8), ch = ci % (kD / 8);
-        const int tk = t * kBN + tt;
-        const bool ok = tk < kv_end;
-        const int64_t off = ok ? (static_cast<int64_t>(q0 + tk) * p.Hkv + hkv) * kD + ch * 8 : 0;
-        const uint32_t so = buf * kKVBytes + (ch >> 3) * (kBN * 128) + sw_off(tt, ch & 7);
-        cp_async16(smem_u32(ks + so), ok ? (const void*)(kg + off) : (const void*)kg, ok);
-        cp_async16(smem_u32(vs + so), ok ? (const void*)(vg + off) : (const void*)vg, ok);
-      }
-      cp_async_arrive(bar_kv(t));
-    }
-  };
-  for (int t = 0; t < kNBuf - 1 && t < n_tiles; ++t) load_tile(t);
-
-  constexpr bool kBf16 = SplitP<T>::value;
-  const uint32_t id_s = tc::idesc_f16(kBf16, false, false, kBM, kBN);
-  const uint32_t id_o = tc::idesc_f16(kBf16, false, true, kBM, kD);
-  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
   const uint32_t t_o = tmem + 2u * kBN;
   auto t_s = [&](int j) { return tmem + static_cast<uint32_t>((j & 1) * kBN); };
+  constexpr bool kBf16 = SplitP<T>::value;
 
-  auto issue_s = [&](int j) {  // S(j) = Q K(j)^T
-    tc::tc_fence_after();
-    const uint32_t qa = smem_u32(qs), kb = smem_u32(ks + (j % kNBuf) * kKVBytes);
+  if (warp >= kLoadWarp) {
+    // =================== producer warps: loads (warp 8), MMA issue (warp 9) ===================
+    // K (which = 0) or V (which = 1) of tile t into its ring buffer
+    auto load_kv = [&](int t, int which) {
+      uint8_t* base = which == 0 ? ks + (t % kNK) * kKVBytes : vs + (t % kNV) * kKVBytes;
+      const uint32_t bar = which == 0 ? k_full(t) : v_full(t);
+      if constexpr (PAGED) {
+        // lane (pg, db) = (lane >> 1, lane & 1) issues the box of page pg, head_dim half db
+        const CUtensorMap* map = which == 0 ? &args.tmap_k : &args.tmap_v;
+        const int pg0 = t * (kBN / kPage);
+        const int npg = min(kBN / kPage, (kv_end - pg0 * kPage + kPage - 1) / kPage);
+        if (lane == 0) mbar_expect_tx(bar, static_cast<uint32_t>(npg * kDB * kPage * 128));
+        __syncwarp();
+        if (lane < npg * kDB) {
+          const int pg = lane >> 1, db = lane & 1;
+          const int idx = pg0 + pg;
+          const int page = idx < kMaxPagesSmem ? s_pages[idx] : __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + idx);
+          tma_load_4d(smem_u32(base + db * (kBN * 128) + pg * kPage * 128), map, db * 64, hkv, 0, page, bar);
+        }
+      } else {
+        const T* src0 = which == 0 ? kg : vg;
+        for (int ci = lane; ci < kBN * (kD / 8); ci += 32) {
+          const int tt = ci / (kD / 8), ch = ci % (kD / 8);
+          const int tk = t * kBN + tt;
+          const bool ok = tk < kv_end;
+          const int64_t off = ok ? (static_cast<int64_t>(q0 + tk) * p.Hkv + hkv) * kD + ch * 8 : 0;
+          cp_async16(smem_u32(base + (ch >> 3) * (kBN * 128) + sw_off(tt, ch & 7)),
+                     ok ? (const void*)(src0 + off) : (const void*)src0, ok);
+        }
+        cp_async_arrive(bar);
+      }
+    };
+    const uint32_t id_s = tc::idesc_f16(kBf16, false, false, kBM, kBN);
+    const uint32_t id_o = tc::idesc_f16(kBf16, false, true, kBM, kD);
+    // Descriptors are built once; per k-step only the start-address field (bits
+    // 0-13, address >> 4) advances, which stays inside the field for smem < 256 KB.
+    const uint64_t dq0 = tc::smem_desc_sw128(smem_u32(qs), 16, 1024);
+    const uint64_t dk0 = tc::smem_desc_sw128(smem_u32(ks), 16, 1024);
+    const uint64_t dv0 = tc::smem_desc_sw128(smem_u32(vs), kBN * 128, 1024);
+    const uint64_t dp0 = tc::smem_desc_sw128(smem_u32(ps), 16, 1024);
+    auto issue_s = [&](int j) {  // S(j) = Q K(j)^T
+      tc::tc_fence_after();
+      const uint64_t kb = dk0 + static_cast<uint64_t>(((j % kNK) * kKVBytes) >> 4);
 #pragma unroll
-    for (int kk = 0; kk < kD / 16; ++kk) {
-      const uint32_t koff = (kk & 3) * 32;
-      const uint64_t ad = tc::smem_desc_sw128(qa + (kk >> 2) * (kBM * 128) + koff, 16, 1024);
-      const uint64_t bd = tc::smem_desc_sw128(kb + (kk >> 2) * (kBN * 128) + koff, 16, 1024);
-      tc::mma_f16(t_s(j), ad, bd, id_s, kk > 0 ? 1u : 0u);
-    }
-    tc::mma_commit(bar_s(j));
-  };
-  auto issue_o = [&](int j) {  // O += P(j) V(j)  (bf16: hi part then lo part)
-    tc::tc_fence_after();
-    const uint32_t vb = smem_u32(vs + (j % kNBuf) * kKVBytes);
-    const int parts = kBf16 ? 2 : 1;
-    for (int part = 0; part < parts; ++part) {
-      const uint32_t pa = smem_u32(part == 0 ? ph : pl);
+      for (int kk = 0; kk < kD / 16; ++kk) {
+        const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4);
+        const uint64_t kboff = static_cast<uint64_t>(((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4);
+        tc::mma_f16(t_s(j), dq0 + koff, kb + kboff, id_s, kk > 0 ? 1u : 0u);
+      }
+      tc::mma_commit(s_full(j));
+    };
+    auto issue_o = [&](int j) {  // O += P(j) V(j)  (bf16: hi part then lo part)
+      tc::tc_fence_after();
+      const uint64_t vb = dv0 + static_cast<uint64_t>(((j % kNV) * kKVBytes) >> 4);
+      const uint64_t pb = dp0 + static_cast<uint64_t>(((j & 1) * kPBufBytes) >> 4);
+      const int parts = kBf16 ? 2 : 1;
+      for (int part = 0; part < parts; ++part) {
+        const uint64_t pa = pb + static_cast<uint64_t>((part * kPBytes) >> 4);
 #pragma unroll
-      for (int kk = 0; kk < kBN / 16; ++kk) {
-        const uint64_t ad = tc::smem_desc_sw128(pa + kk * 32, 16, 1024);
-        const uint64_t bd = tc::smem_desc_sw128(vb + kk * 16 * 128, kBN * 128, 1024);
-        tc::mma_f16(t_o, ad, bd, id_o, (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          tc::mma_f16(t_o, pa + static_cast<uint64_t>((kk * 32) >> 4), vb + static_cast<uint64_t>((kk * 16 * 128) >> 4),
+                      id_o, (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+      }
+      tc::mma_commit(o_done(j));
+    };
+    bool ok = true;
+    if (warp == kLoadWarp) {
+      for (int t = 0; t < kNK - 1 && t < n_tiles; ++t) load_kv(t, 0);
+      for (int t = 0; t < kNV - 1 && t < n_tiles; ++t) load_kv(t, 1);
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + kNK - 1 < n_tiles) {  // K buffer of tile j-1: free once S(j-1) completed
+          if (j >= 1) ok = tc::mbar_wait(k_free(j - 1), ((j - 1) / kNK) & 1);
+          if (!ok) break;
+          load_kv(j + kNK - 1, 0);
+        }
+        if (j + kNV - 1 < n_tiles) {  // V buffer of tile j-1: free once PV(j-1) completed
+          if (j >= 1) ok = tc::mbar_wait(v_free(j - 1), ((j - 1) / kNV) & 1);
+          if (!ok) break;
+          load_kv(j + kNV - 1, 1);
+        }
+        __syncwarp();
+      }
+    } else {
+      if (n_tiles > 0) {
+        ok = tc::mbar_wait(k_full(0), 0);
+        if (ok && lane == 0) {
+          issue_s(0);
+          tc::mma_commit(k_free(0));
+        }
+      }
+      for (int j = 0; ok && j < n_tiles; ++j) {
+        if (j + 1 < n_tiles) {
+          ok = tc::mbar_wait(k_full(j + 1), ((j + 1) / kNK) & 1);
+          if (!ok) break;
+          if (lane == 0) {
+            issue_s(j + 1);
+            tc::mma_commit(k_free(j + 1));
+          }
+        }
+        ok = tc::mbar_wait(p_full(j), (j >> 1) & 1);  // softmax(j) wrote P(j), done with S(j)
+        if (!ok) break;
+        ok = tc::mbar_wait(v_full(j), (j / kNV) & 1);
+        if (!ok) break;
+        if (lane == 0) {
+          issue_o(j);
+          tc::mma_commit(v_free(j));
+        }
+        __syncwarp();
       }
     }
-    tc::mma_commit(bar_o(j));
-  };
-
-  cp_async_wait<0>();  // Q (and, dense path, the prologue tiles) resident
-  tc::fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0 && n_tiles > 0) {
-    if (!tc::mbar_wait(bar_kv(0), 0)) *s_fail = 1;
-    else issue_s(0);
-  }
-
-  const int row = tid;
-  const int tok = tok0 + row / p.n_rep;
-  const int lim = p.causal ? (tok < nq ? sk - nq + tok : sk - 1) : sk - 1;
-  float m_ref = -INFINITY, l_run = 0.f;
-  bool failed = false;
-
-  for (int it = 0; it < n_tiles; ++it) {
-    // [A] next tile's S on the tensor core while this tile's softmax runs
-    if (tid == 0 && it + 1 < n_tiles) {
-      if (!tc::mbar_wait(bar_kv(it + 1), ((it + 1) / kNBuf) & 1)) *s_fail = 1;
-      else issue_s(it + 1);
-    }
-    // [B] S(it) ready; O(it-1) accumulated (frees P, the K/V buffer of it-1, and O for a rescale)
-    bool ok = tc::mbar_wait(bar_s(it), (it >> 1) & 1);
-    if (it > 0) ok = ok && tc::mbar_wait(bar_o(it - 1), ((it - 1) >> 1) & 1);
-    if (__syncthreads_or(!ok || *s_fail)) {
-      failed = true;
-      break;
-    }
-    tc::tc_fence_after();
-    if (it + kNBuf - 1 < n_tiles) load_tile(it + kNBuf - 1);  // into the buffer tile it-1 used
-
-    float s[kBN];
-    tc::tmem_ld32(t_s(it) + lane_base, s);
-    tc::tmem_ld32(t_s(it) + lane_base + 32, s + 32);
-    const int tbase = it * kBN;
-    float mx = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < kBN; ++c) {
-      s[c] = (tbase + c <= lim) ? s[c] * p.scale_log2 : -INFINITY;
-      mx = fmaxf(mx, s[c]);
-    }
-    // lazy reference max: move it (and rescale O, l) only when the row max grew by > threshold
-    const bool need = mx > m_ref + kRescaleThreshold;
-    float alpha = 1.f;
-    if (need) {
-      alpha = fast_exp2(m_ref - mx);  // 0 when m_ref = -inf
-      m_ref = mx;
-      l_run *= alpha;
-    }
-    if (it > 0 && __any_sync(0xffffffffu, need)) {
-#pragma unroll
-      for (int c0 = 0; c0 < kD; c0 += 32) {
-        float o[32];
-        tc::tmem_ld32(t_o + lane_base + c0, o);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] *= alpha;
-        tmem_st32(t_o + lane_base + c0, o);
-      }
-    }
-    const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-    float sum = 0.f;
-#pragma unroll
-    for (int c = 0; c < kBN; c += 8) {
-      uint32_t hi[4], lo[4];
-#pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        const float a = fast_exp2(s[c + e] - m_use), bb = fast_exp2(s[c + e + 1] - m_use);
-        sum += a + bb;
-        split2<T>(a, bb, hi[e >> 1], lo[e >> 1]);
-      }
-      const uint32_t off = sw_off(row, c >> 3);
-      *reinterpret_cast<uint4*>(ph + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-      if (kBf16) *reinterpret_cast<uint4*>(pl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    }
-    l_run += sum;
-
-    if (it == n_tiles - 1 && kv_end < (it + 1) * kBN) {
-      // rows of the last page past kv_end hold whatever the pool page holds (P is 0
-      // there, but 0 * NaN is not): zero them in the V tile once it has landed
-      const bool okv = tc::mbar_wait(bar_kv(it), (it / kNBuf) & 1);
-      if (!okv) *s_fail = 1;
-      uint8_t* vb = vs + (it % kNBuf) * kKVBytes;
-      const int first = kv_end - it * kBN;
-      for (int e = tid; e < (kBN - first) * kDB * 8; e += 128) {
-        const int tt = first + e / (kDB * 8), rem = e % (kDB * 8);
-        *reinterpret_cast<uint4*>(vb + (rem >> 3) * (kBN * 128) + tt * 128 + (rem & 7) * 16) = make_uint4(0, 0, 0, 0);
-      }
-    }
-    tc::fence_proxy_async_smem();  // P (and zeroed V rows) -> visible to the tensor core
-    tc::tc_fence_before();
-    // barrier + uniform failure vote (the flag is only ever read through the vote)
-    if (__syncthreads_or(*s_fail)) {
-      failed = true;
-      break;
-    }
-    if (tid == 0) issue_o(it);
-  }
-  if (!failed && n_tiles > 0) {
-    const int last = n_tiles - 1;
-    const bool ok = tc::mbar_wait(bar_o(last), (last >> 1) & 1);
-    if (__syncthreads_or(!ok)) failed = true;
-  }
-  tc::tc_fence_after();
-  cp_async_wait<0>();
-
-  // ---- epilogue: O / l from TMEM ----
-  float acc[kD];
-  if (!failed && n_tiles > 0) {
-#pragma unroll
-    for (int c0 = 0; c0 < kD; c0 += 32) tc::tmem_ld32(t_o + lane_base + c0, acc + c0);
+    if (!ok) *s_fail = 1;
   } else {
+    // ============ softmax warps: two threads per accumulator row ============
+    // warp w handles rows (w % 4)*32 + lane (TMEM lanes of its sub-partition) and
+    // the column half w / 4: S columns [32h, 32h+32), O columns [64h, 64h+64).
+    const int half = warp / 4;
+    const int row = (warp % 4) * 32 + lane;
+    const int tok = tok0 + row / p.n_rep;
+    const int lim = p.causal ? (tok < nq ? sk - nq + tok : sk - 1) : sk - 1;
+    const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
+    const int sc0 = half * (kBN / 2), oc0 = half * (kD / 2);
+    float m_ref = -INFINITY, l_run = 0.f;
+    // A failed (timed-out) wait only sets `failed`: the loop keeps its shape, so
+    // every softmax warp still reaches every named barrier, and later waits are
+    // skipped; the rows are then written as NaN.
+    bool failed = false;
+    auto wait = [&](uint32_t bar, uint32_t parity) {
+      if (failed) return;
+#ifdef BPKV_TRACE
+      BPKV_T0();
+#endif
+      const bool r = tc::mbar_wait(bar, parity);
+#ifdef BPKV_TRACE
+      if (BPKV_TRACING && tid == 0) BPKV_TADD(4);
+#endif
+      if (!__all_sync(0xffffffffu, r)) failed = true;
+    };
+#ifdef BPKV_TRACE
+    const long long _tstart = clock64();
+#endif
+    for (int it = 0; it < n_tiles; ++it) {
+      wait(s_full(it), (it >> 1) & 1);
+      tc::tc_fence_after();
+      float s[kBN / 2];
+      tc::tmem_ld32(t_s(it) + lane_base + sc0, s);
+      const int tbase = it * kBN + sc0;
+      float mxh = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < kD; ++i) acc[i] = 0.f;
-  }
-  if (tok < nq) {
-    const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-    const float nan = __int_as_float(0x7fc00000);
-    T* dst = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(q0 + tok) * p.Hq + hkv * p.n_rep + row % p.n_rep) * kD;
+      for (int c = 0; c < kBN / 2; ++c) {
+        s[c] = (tbase + c <= lim) ? s[c] : -INFINITY;
+        mxh = fmaxf(mxh, s[c]);
+      }
+      // exchange the half-row maxima (double-buffered; named barrier of the softmax warps)
+      s_mx[((it & 1) * 2 + half) * kBM + row] = mxh;
+      {
+#ifdef BPKV_TRACE
+        BPKV_T0();
+#endif
+        asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kSoftmaxWarps) : "memory");
+#ifdef BPKV_TRACE
+        if (BPKV_TRACING && tid == 0) BPKV_TADD(5);
+#endif
+      }
+      const float mx = fmaxf(s_mx[((it & 1) * 2 + 0) * kBM + row], s_mx[((it & 1) * 2 + 1) * kBM + row]) * p.scale_log2;
+      // lazy reference max: move it (rescale O, l) only when the row max grew by > threshold
+      const bool need = mx > m_ref + kRescaleThreshold;
+      float alpha = 1.f;
+      if (need) {
+        alpha = fast_exp2(m_ref - mx);  // 0 when m_ref = -inf
+        m_ref = mx;
+        l_run *= alpha;
+      }
+      if (it > 0 && __any_sync(0xffffffffu, need)) {
+        wait(o_done(it - 1), ((it - 1) >> 1) & 1);  // O last written by PV(it-1)
+        tc::tc_fence_after();
 #pragma unroll
-    for (int c = 0; c < kD; c += 8) {
-      float v[8];
+        for (int c0 = 0; c0 < kD / 2; c0 += 32) {
+          float o[32];
+          tc::tmem_ld32(t_o + lane_base + oc0 + c0, o);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = failed ? nan : acc[c + i] * inv;
-      *reinterpret_cast<uint4*>(dst + c) =
-          make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]), pack2<T>(v[6], v[7]));
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(t_o + lane_base + oc0 + c0, o);
+        }
+      }
+      if (it >= 2) {  // P buffer it&1 was last read by PV(it-2)
+        wait(o_done(it - 2), ((it - 2) >> 1) & 1);
+      }
+      const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
+      uint8_t* ph = p_hi(it);
+      uint8_t* pl = p_lo(it);
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < kBN / 2; c += 8) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          const float a = fast_exp2(fmaf(s[c + e], p.scale_log2, -m_use));
+          const float bb = fast_exp2(fmaf(s[c + e + 1], p.scale_log2, -m_use));
+          sum += a + bb;
+          split2<T>(a, bb, hi[e >> 1], lo[e >> 1]);
+        }
+        const uint32_t off = sw_off(row, (sc0 + c) >> 3);
+        *reinterpret_cast<uint4*>(ph + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        if (kBf16) *reinterpret_cast<uint4*>(pl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+      l_run += sum;
+      if (it == n_tiles - 1 && kv_end < (it + 1) * kBN) {
+        // rows of the last page past kv_end hold whatever the pool page holds (P is
+        // 0 there, but 0 * NaN is not): zero them in the V tile once it has landed
+        wait(v_full(it), (it / kNV) & 1);
+        uint8_t* vb = vs + (it % kNV) * kKVBytes;
+        const int first = kv_end - it * kBN;
+        for (int e = tid; e < (kBN - first) * kDB * 8; e += 32 * kSoftmaxWarps) {
+          const int tt = first + e / (kDB * 8), rem = e % (kDB * 8);
+          *reinterpret_cast<uint4*>(vb + (rem >> 3) * (kBN * 128) + tt * 128 + (rem & 7) * 16) =
+              make_uint4(0, 0, 0, 0);
+        }
+      }
+      tc::fence_proxy_async_smem();  // P (and zeroed V rows) -> visible to the tensor core
+      tc::tc_fence_before();
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(p_full(it)) : "memory");
+    }
+    if (n_tiles > 0) wait(o_done(n_tiles - 1), ((n_tiles - 1) >> 1) & 1);
+#ifdef BPKV_TRACE
+    if (BPKV_TRACING && tid == 0) {
+      atomicAdd(&g_prefill_trace[6], static_cast<unsigned long long>(clock64() - _tstart));
+      atomicAdd(&g_prefill_trace[7], static_cast<unsigned long long>(n_tiles));
+    }
+#endif
+    if (failed) *s_fail = 1;
+    const bool ok = !failed;
+    // ---- epilogue: row sum of both halves, O / l from TMEM ----
+    s_l[half * kBM + row] = l_run;
+    asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kSoftmaxWarps) : "memory");
+    const float l_row = s_l[row] + s_l[kBM + row];
+    float acc[kD / 2];
+    const bool all_ok = __all_sync(0xffffffffu, ok);  // before any divergent branch
+    if (all_ok && n_tiles > 0) {
+      tc::tc_fence_after();
+#pragma unroll
+      for (int c0 = 0; c0 < kD / 2; c0 += 32) tc::tmem_ld32(t_o + lane_base + oc0 + c0, acc + c0);
+    } else {
+#pragma unroll
+      for (int i = 0; i < kD / 2; ++i) acc[i] = 0.f;
+    }
+    if (tok < nq) {
+      const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+      const float nan = __int_as_float(0x7fc00000);
+      T* dst = reinterpret_cast<T*>(p.out) +
+               (static_cast<int64_t>(q0 + tok) * p.Hq + hkv * p.n_rep + row % p.n_rep) * kD + oc0;
+#pragma unroll
+      for (int c = 0; c < kD / 2; c += 8) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = all_ok ? acc[c + i] * inv : nan;
+        *reinterpret_cast<uint4*>(dst + c) =
+            make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]), pack2<T>(v[6], v[7]));
+      }
     }
   }
+  cp_async_wait<0>();
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -431,7 +528,7 @@ int prefill_tc_launch(PrefillTcParams& p, int head_dim, int dtype, int max_seqle
       }                                                                                                    \
       raised[variant][dev] = true;                                                                         \
     }                                                                                                      \
-    kern<<<grid, 128, kSmemBytes, st>>>(args);                                                             \
+    kern<<<grid, kThreads, kSmemBytes, st>>>(args);                                                             \
   } while (0)
   if (dtype == BPKV_BF16) {
     if (paged) BPKV_TC_LAUNCH(__nv_bfloat16, true); else BPKV_TC_LAUNCH(__nv_bfloat16, false);
@@ -443,3 +540,15 @@ int prefill_tc_launch(PrefillTcParams& p, int head_dim, int dtype, int max_seqle
 }
 
 }  // namespace bpkv
+
+#ifdef BPKV_TRACE
+extern "C" BPKV_API int bpkv_debug_prefill_trace(unsigned long long* out, int n, int reset) {
+  if (n > 16) n = 16;
+  if (cudaMemcpyFromSymbol(out, bpkv::g_prefill_trace, sizeof(unsigned long long) * n) != cudaSuccess) return 3;
+  if (reset) {
+    unsigned long long z[16] = {0};
+    cudaMemcpyToSymbol(bpkv::g_prefill_trace, z, sizeof(z));
+  }
+  return 0;
+}
+#endif

@@ -46,19 +46,6 @@ __device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
   asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
 }
 
-// TMEM -> registers: 32 lanes x 16 consecutive 32-bit columns (load + wait in one statement)
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
-      "tcgen05.wait::ld.sync.aligned;\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 // Q rows of group g (row = r*Wp + i, zero for i >= W or row >= rows) -> [db][row][128 B]
 template <typename T>
 __device__ void load_q(const ScoreTcParams& p, uint8_t* qs, int g, int rows_pad, int nthr) {
@@ -265,7 +252,7 @@ __global__ void __launch_bounds__(128, 2) score_tokens_tc_kernel(ScoreTcParams p
       for (int i0 = 0; i0 < p.Wp; i0 += 16) {
         const int c0 = r * p.Wp + i0;
         float sv[16];
-        tmem_ld16(base + c0, sv);
+        tc::tmem_ld16(base + c0, sv);
 #pragma unroll
         for (int i = 0; i < 16; ++i) cur += fast_exp2(fmaf(sv[i], p.scale_log2, -s_off[c0 + i]));
       }

@@ -57,17 +57,19 @@ constexpr int kD = 128, kBM = 128, kBN = 64, kDB = kD / 64;
 constexpr int kQBytes = kDB * kBM * 128;       // 32 KB
 constexpr int kKVBytes = kDB * kBN * 128;      // 16 KB per K or V tile
 constexpr int kPBytes = kBM * 128;             // 16 KB (64 tokens per row)
-constexpr int kNK = 4;                         // K ring depth (K(j) is free once S(j) was consumed)
-constexpr int kNV = 3;                         // V ring depth (V(j) is free once PV(j) completed)
+constexpr int kNK = 6;                         // K ring depth (K(j) is free once S(j) completed)
+constexpr int kNV = 5;                         // V ring depth (V(j) is free once PV(j) completed)
 constexpr int kPBufBytes = 2 * kPBytes;        // one P buffer: hi + lo parts
-constexpr int kSoftmaxWarps = 8;               // warps 0-7: softmax (two per row group)
+constexpr int kSplit = 4;                      // softmax threads per accumulator row
+constexpr int kSoftmaxWarps = 4 * kSplit;      // warps 0..15: softmax
 constexpr int kLoadWarp = kSoftmaxWarps;       // warp 8: TMA / cp.async loads
 constexpr int kMmaWarp = kSoftmaxWarps + 1;    // warp 9: tcgen05.mma issue
 constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
 constexpr int kMaxPagesSmem = 2048;            // block-table entries staged in shared memory
-constexpr int kSmemBytes = kQBytes + (kNK + kNV) * kKVBytes + 2 * kPBufBytes + 1024 /*align*/ + 256 + 4 * kMaxPagesSmem +
-                            4 * 2 * 2 * kBM /*row-max exchange*/ + 4 * 2 * kBM /*row sums*/;
-constexpr uint32_t kTmemCols = 256;            // S0 [0,64) S1 [64,128) O [128,256)
+constexpr int kSmemBytes = (kNK + kNV) * kKVBytes + 1024 /*align*/ + 256 + 4 * kMaxPagesSmem +
+                            4 * 2 * kSplit * kBM /*row-max exchange*/ + 4 * kSplit * kBM /*row sums*/;
+constexpr uint32_t kTmemCols = 512;            // S0 [0,64) S1 [64,128) O [128,256) Q [256,320) P [320,448)
+constexpr uint32_t kTmemQ = 256, kTmemP = 320;  // bf16 pairs per 32-bit column
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 256 between rescales
 
 struct __align__(64) TcKernelArgs {
@@ -112,17 +114,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   const PrefillTcParams& p = args.p;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* qs = smem;
-  uint8_t* ks = qs + kQBytes;            // kNK buffers
+  uint8_t* ks = smem;                    // kNK buffers
   uint8_t* vs = ks + kNK * kKVBytes;     // kNV buffers
-  uint8_t* ps = vs + kNV * kKVBytes;     // 2 P buffers, each hi + lo
-  uint64_t* bars = reinterpret_cast<uint64_t*>(ps + 2 * kPBufBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(vs + kNV * kKVBytes);
   // bars: k_full[kNK], v_full[kNV], s_full[2], p_full[2], o_done[2], k_free[kNK], v_free[kNV]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * (kNK + kNV) + 6);
   int* s_fail = reinterpret_cast<int*>(tmem_slot + 1);
   int* s_pages = reinterpret_cast<int*>(bars + 32);
-  float* s_mx = reinterpret_cast<float*>(s_pages + kMaxPagesSmem);  // [2 buffers][2 halves][kBM]
-  float* s_l = s_mx + 4 * kBM;                                         // [2 halves][kBM]
+  float* s_mx = reinterpret_cast<float*>(s_pages + kMaxPagesSmem);  // [2 buffers][kSplit parts][kBM]
+  float* s_l = s_mx + 2 * kSplit * kBM;                                // [kSplit parts][kBM]
 
   const int b = blockIdx.x / p.tiles_per_req;
   const int qt = blockIdx.x % p.tiles_per_req;
@@ -144,8 +144,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   auto o_done = [&](int j) { return smem_u32(&bars[kNK + kNV + 4 + (j & 1)]); };
   auto k_free = [&](int t) { return smem_u32(&bars[kNK + kNV + 6 + t % kNK]); };
   auto v_free = [&](int t) { return smem_u32(&bars[2 * kNK + kNV + 6 + t % kNV]); };
-  auto p_hi = [&](int j) { return ps + (j & 1) * kPBufBytes; };
-  auto p_lo = [&](int j) { return ps + (j & 1) * kPBufBytes + kPBytes; };
 
   if (warp == 0) {
     tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
@@ -164,15 +162,6 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     tc::fence_mbar_init();
   }
 
-  // ---- Q tile: row m = (token tok0 + m / n_rep, head m % n_rep), all threads ----
-  for (int ci = tid; ci < kBM * (kD / 8); ci += kThreads) {
-    const int m = ci / (kD / 8), ch = ci % (kD / 8);
-    const int tok = tok0 + m / p.n_rep, r = m % p.n_rep;
-    const bool ok = tok < nq;
-    const T* src = qg + (static_cast<int64_t>(q0 + tok) * p.Hq + hkv * p.n_rep + r) * kD + ch * 8;
-    cp_async16(smem_u32(qs + (ch >> 3) * (kBM * 128) + sw_off(m, ch & 7)), ok ? (const void*)src : (const void*)qg, ok);
-  }
-  cp_async_commit();
   const int last_tok = min(tok0 + TQ, nq) - 1;
   const int kv_end = p.causal ? min(sk, sk - nq + last_tok + 1) : sk;
   const int n_tiles = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
@@ -180,12 +169,34 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const int np = min((kv_end + kPage - 1) / kPage, kMaxPagesSmem);
     for (int i = tid; i < np; i += kThreads) s_pages[i] = __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + i);
   }
-  cp_async_wait<0>();
-  tc::fence_proxy_async_smem();
   tc::tc_fence_before();
-  __syncthreads();  // Q resident, barriers initialised, TMEM address published, block table staged
+  __syncthreads();  // barriers initialised, TMEM address published, block table staged
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // ---- Q tile -> TMEM (A operand of S = Q K^T): row m = (token tok0 + m / n_rep, head m % n_rep),
+  //      lane m, 32-bit column k/2 holds q[m][k], q[m][k+1] ----
+  if (warp < 4) {
+    const int m = tid;
+    const int tq = tok0 + m / p.n_rep, r = m % p.n_rep;
+    const uint4* src = reinterpret_cast<const uint4*>(qg + (static_cast<int64_t>(q0 + tq) * p.Hq + hkv * p.n_rep + r) * kD);
+    const uint32_t qlane = static_cast<uint32_t>(warp * 32) << 16;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t u[32];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint4 v = tq < nq ? __ldg(src + half * 8 + i) : make_uint4(0, 0, 0, 0);
+        u[4 * i] = v.x;
+        u[4 * i + 1] = v.y;
+        u[4 * i + 2] = v.z;
+        u[4 * i + 3] = v.w;
+      }
+      tc::tmem_st32u(tmem + kTmemQ + qlane + half * 32, u);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();  // Q resident in TMEM
+  tc::tc_fence_after();
   const uint32_t t_o = tmem + 2u * kBN;
   auto t_s = [&](int j) { return tmem + static_cast<uint32_t>((j & 1) * kBN); };
   constexpr bool kBf16 = SplitP<T>::value;
@@ -226,32 +237,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const uint32_t id_o = tc::idesc_f16(kBf16, false, true, kBM, kD);
     // Descriptors are built once; per k-step only the start-address field (bits
     // 0-13, address >> 4) advances, which stays inside the field for smem < 256 KB.
-    const uint64_t dq0 = tc::smem_desc_sw128(smem_u32(qs), 16, 1024);
     const uint64_t dk0 = tc::smem_desc_sw128(smem_u32(ks), 16, 1024);
     const uint64_t dv0 = tc::smem_desc_sw128(smem_u32(vs), kBN * 128, 1024);
-    const uint64_t dp0 = tc::smem_desc_sw128(smem_u32(ps), 16, 1024);
-    auto issue_s = [&](int j) {  // S(j) = Q K(j)^T
+    auto issue_s = [&](int j) {  // S(j) = Q K(j)^T, Q from TMEM
       tc::tc_fence_after();
       const uint64_t kb = dk0 + static_cast<uint64_t>(((j % kNK) * kKVBytes) >> 4);
 #pragma unroll
       for (int kk = 0; kk < kD / 16; ++kk) {
-        const uint64_t koff = static_cast<uint64_t>(((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4);
         const uint64_t kboff = static_cast<uint64_t>(((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4);
-        tc::mma_f16(t_s(j), dq0 + koff, kb + kboff, id_s, kk > 0 ? 1u : 0u);
+        tc::mma_f16_ts(t_s(j), tmem + kTmemQ + kk * 8, kb + kboff, id_s, kk > 0 ? 1u : 0u);
       }
       tc::mma_commit(s_full(j));
     };
-    auto issue_o = [&](int j) {  // O += P(j) V(j)  (bf16: hi part then lo part)
+    auto issue_o = [&](int j) {  // O += P(j) V(j), P from TMEM (bf16: hi part then lo part)
       tc::tc_fence_after();
       const uint64_t vb = dv0 + static_cast<uint64_t>(((j % kNV) * kKVBytes) >> 4);
-      const uint64_t pb = dp0 + static_cast<uint64_t>(((j & 1) * kPBufBytes) >> 4);
       const int parts = kBf16 ? 2 : 1;
       for (int part = 0; part < parts; ++part) {
-        const uint64_t pa = pb + static_cast<uint64_t>((part * kPBytes) >> 4);
+        const uint32_t pa = tmem + kTmemP + (j & 1) * 64 + part * 32;
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
-          tc::mma_f16(t_o, pa + static_cast<uint64_t>((kk * 32) >> 4), vb + static_cast<uint64_t>((kk * 16 * 128) >> 4),
-                      id_o, (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+          tc::mma_f16_ts(t_o, pa + kk * 8, vb + static_cast<uint64_t>((kk * 16 * 128) >> 4), id_o,
+                         (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
       }
       tc::mma_commit(o_done(j));
     };
@@ -302,15 +309,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     }
     if (!ok) *s_fail = 1;
   } else {
-    // ============ softmax warps: two threads per accumulator row ============
+    // ============ softmax warps: kSplit threads per accumulator row ============
     // warp w handles rows (w % 4)*32 + lane (TMEM lanes of its sub-partition) and
-    // the column half w / 4: S columns [32h, 32h+32), O columns [64h, 64h+64).
+    // column part h = w / 4: S columns [h*kBN/kSplit, ...), O columns [h*kD/kSplit, ...).
     const int half = warp / 4;
     const int row = (warp % 4) * 32 + lane;
     const int tok = tok0 + row / p.n_rep;
     const int lim = p.causal ? (tok < nq ? sk - nq + tok : sk - 1) : sk - 1;
     const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
-    const int sc0 = half * (kBN / 2), oc0 = half * (kD / 2);
+    constexpr int kSC = kBN / kSplit, kOC = kD / kSplit;
+    const int sc0 = half * kSC, oc0 = half * kOC;
     float m_ref = -INFINITY, l_run = 0.f;
     // A failed (timed-out) wait only sets `failed`: the loop keeps its shape, so
     // every softmax warp still reaches every named barrier, and later waits are
@@ -333,17 +341,30 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     for (int it = 0; it < n_tiles; ++it) {
       wait(s_full(it), (it >> 1) & 1);
       tc::tc_fence_after();
-      float s[kBN / 2];
-      tc::tmem_ld32(t_s(it) + lane_base + sc0, s);
+      float s[kSC];
+#ifdef BPKV_TRACE
+      long long _tl = clock64();
+#endif
+      tc::tmem_ld16(t_s(it) + lane_base + sc0, s);
+#ifdef BPKV_TRACE
+      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[8], static_cast<unsigned long long>(clock64() - _tl));
+      _tl = clock64();
+#endif
       const int tbase = it * kBN + sc0;
-      float mxh = -INFINITY;
+      if (tbase + kSC - 1 > lim) {  // only tiles that cross this row's causal limit need the mask
 #pragma unroll
-      for (int c = 0; c < kBN / 2; ++c) {
-        s[c] = (tbase + c <= lim) ? s[c] : -INFINITY;
-        mxh = fmaxf(mxh, s[c]);
+        for (int c = 0; c < kSC; ++c) s[c] = (tbase + c <= lim) ? s[c] : -INFINITY;
       }
+      float mx4[4] = {s[0], s[1], s[2], s[3]};  // four independent max chains
+#pragma unroll
+      for (int c = 4; c < kSC; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+      const float mxh = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+#ifdef BPKV_TRACE
+      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[11], static_cast<unsigned long long>(clock64() - _tl));
+      _tl = clock64();
+#endif
       // exchange the half-row maxima (double-buffered; named barrier of the softmax warps)
-      s_mx[((it & 1) * 2 + half) * kBM + row] = mxh;
+      s_mx[((it & 1) * kSplit + half) * kBM + row] = mxh;
       {
 #ifdef BPKV_TRACE
         BPKV_T0();
@@ -353,7 +374,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         if (BPKV_TRACING && tid == 0) BPKV_TADD(5);
 #endif
       }
-      const float mx = fmaxf(s_mx[((it & 1) * 2 + 0) * kBM + row], s_mx[((it & 1) * 2 + 1) * kBM + row]) * p.scale_log2;
+      float mxr = s_mx[((it & 1) * kSplit) * kBM + row];
+#pragma unroll
+      for (int h = 1; h < kSplit; ++h) mxr = fmaxf(mxr, s_mx[((it & 1) * kSplit + h) * kBM + row]);
+      const float mx = mxr * p.scale_log2;
+#ifdef BPKV_TRACE
+      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[12], static_cast<unsigned long long>(clock64() - _tl));
+      _tl = clock64();
+#endif
       // lazy reference max: move it (rescale O, l) only when the row max grew by > threshold
       const bool need = mx > m_ref + kRescaleThreshold;
       float alpha = 1.f;
@@ -366,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         wait(o_done(it - 1), ((it - 1) >> 1) & 1);  // O last written by PV(it-1)
         tc::tc_fence_after();
 #pragma unroll
-        for (int c0 = 0; c0 < kD / 2; c0 += 32) {
+        for (int c0 = 0; c0 < kOC; c0 += 32) {
           float o[32];
           tc::tmem_ld32(t_o + lane_base + oc0 + c0, o);
 #pragma unroll
@@ -374,28 +402,41 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           tmem_st32(t_o + lane_base + oc0 + c0, o);
         }
       }
+#ifdef BPKV_TRACE
+      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[13], static_cast<unsigned long long>(clock64() - _tl));
+      _tl = clock64();
+#endif
       if (it >= 2) {  // P buffer it&1 was last read by PV(it-2)
         wait(o_done(it - 2), ((it - 2) >> 1) & 1);
       }
       const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-      uint8_t* ph = p_hi(it);
-      uint8_t* pl = p_lo(it);
-      float sum = 0.f;
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
+      uint32_t hi[kSC / 2], lo[kSC / 2];
 #pragma unroll
-      for (int c = 0; c < kBN / 2; c += 8) {
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const float a = fast_exp2(fmaf(s[c + e], p.scale_log2, -m_use));
-          const float bb = fast_exp2(fmaf(s[c + e + 1], p.scale_log2, -m_use));
-          sum += a + bb;
-          split2<T>(a, bb, hi[e >> 1], lo[e >> 1]);
-        }
-        const uint32_t off = sw_off(row, (sc0 + c) >> 3);
-        *reinterpret_cast<uint4*>(ph + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        if (kBf16) *reinterpret_cast<uint4*>(pl + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      for (int c = 0; c < kSC; c += 2) {
+        const float a = fast_exp2(fmaf(s[c], p.scale_log2, -m_use));
+        const float bb = fast_exp2(fmaf(s[c + 1], p.scale_log2, -m_use));
+        sum4[(c >> 1) & 3] += a + bb;
+        split2<T>(a, bb, hi[c >> 1], lo[c >> 1]);
       }
-      l_run += sum;
+#ifdef BPKV_TRACE
+      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[14], static_cast<unsigned long long>(clock64() - _tl));
+      _tl = clock64();
+#endif
+      // P(it) -> TMEM buffer it&1: 32-bit column = token pair
+      const uint32_t pcol = tmem + kTmemP + (it & 1) * 64 + lane_base + sc0 / 2;
+      static_assert(kSC / 2 == 8, "one x8 store per part");
+      tc::tmem_st8(pcol, hi);
+      if (kBf16) tc::tmem_st8(pcol + 32, lo);
+#ifdef BPKV_TRACE
+      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[15], static_cast<unsigned long long>(clock64() - _tl));
+      _tl = clock64();
+#endif
+      l_run += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+#ifdef BPKV_TRACE
+      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[9], static_cast<unsigned long long>(clock64() - _tl));
+      _tl = clock64();
+#endif
       if (it == n_tiles - 1 && kv_end < (it + 1) * kBN) {
         // rows of the last page past kv_end hold whatever the pool page holds (P is
         // 0 there, but 0 * NaN is not): zero them in the V tile once it has landed
@@ -408,9 +449,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
               make_uint4(0, 0, 0, 0);
         }
       }
-      tc::fence_proxy_async_smem();  // P (and zeroed V rows) -> visible to the tensor core
-      tc::tc_fence_before();
+      tc::fence_proxy_async_smem();  // zeroed V rows -> visible to the tensor core
+      tc::tc_fence_before();       // P stores in TMEM -> ordered before the MMA warp's issue
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(p_full(it)) : "memory");
+#ifdef BPKV_TRACE
+      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[10], static_cast<unsigned long long>(clock64() - _tl));
+#endif
     }
     if (n_tiles > 0) wait(o_done(n_tiles - 1), ((n_tiles - 1) >> 1) & 1);
 #ifdef BPKV_TRACE
@@ -424,16 +468,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     // ---- epilogue: row sum of both halves, O / l from TMEM ----
     s_l[half * kBM + row] = l_run;
     asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kSoftmaxWarps) : "memory");
-    const float l_row = s_l[row] + s_l[kBM + row];
-    float acc[kD / 2];
+    float l_row = 0.f;
+#pragma unroll
+    for (int h = 0; h < kSplit; ++h) l_row += s_l[h * kBM + row];
+    float acc[kOC];
     const bool all_ok = __all_sync(0xffffffffu, ok);  // before any divergent branch
     if (all_ok && n_tiles > 0) {
       tc::tc_fence_after();
 #pragma unroll
-      for (int c0 = 0; c0 < kD / 2; c0 += 32) tc::tmem_ld32(t_o + lane_base + oc0 + c0, acc + c0);
+      for (int c0 = 0; c0 < kOC; c0 += 32) tc::tmem_ld32(t_o + lane_base + oc0 + c0, acc + c0);
     } else {
 #pragma unroll
-      for (int i = 0; i < kD / 2; ++i) acc[i] = 0.f;
+      for (int i = 0; i < kOC; ++i) acc[i] = 0.f;
     }
     if (tok < nq) {
       const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
@@ -441,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       T* dst = reinterpret_cast<T*>(p.out) +
                (static_cast<int64_t>(q0 + tok) * p.Hq + hkv * p.n_rep + row % p.n_rep) * kD + oc0;
 #pragma unroll
-      for (int c = 0; c < kD / 2; c += 8) {
+      for (int c = 0; c < kOC; c += 8) {
         float v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = all_ok ? acc[c + i] * inv : nan;

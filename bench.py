@@ -336,7 +336,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         "tokens_per_s": round(tokens_per_s, 2),
         "hbm_frac_of_measured": round(gbs / world / peak, 4),
         "roofline": {"bound": "hbm", "achieved": round(launch_gbs, 2), "peak": peak, "unit": "GB/s",
-                     "frac": round(launch_gbs / peak, 4), "traffic": None,
+                     "frac": round(launch_gbs / peak, 4),
+                     # dram__bytes_read.sum + dram__bytes_write.sum of one decode launch of this
+                     # workload (ncu capture in profiles/page16_decode_llama8b_config2.md)
+                     "traffic": 2259438000 + 5422080,
+                     "algorithmic_bytes_per_launch": int(bytes_layer),
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                      "kernel": "page16_decode_mma_kernel<bf16,128,8,3> + combine, per layer launch",
                      "avg_launch_ms": round(launch_ms, 4)},
@@ -552,13 +556,118 @@ def run_longseq(args, rank, world, local_rank):
         "hbm_frac_of_measured_per_gpu": round(gbs / world / hbm, 4),
     }), flush=True)
 
+
+def run_mixed(args):
+    """Config 5: 64 active requests per step (Llama-3.1-8B shapes, bf16, 32 layers):
+    56 decoding (ctx lognormal(ln 4000, 0.8) clipped to [256, 32768]) and 8 in
+    chunked prefill (512-token causal chunks over a past drawn the same way, paged
+    KV).  The pool is capped at 40% of HBM.  Cold requests (20% of the decode
+    pages) live in pinned host memory; each step prefetches one of them on the
+    side stream (overlapped, used from the next step on) and offloads one active
+    request, so the batch rotates through the offload engine."""
+    import torch
+    from unifiedkv_b200.chunked_prefill import paged_chunk_prefill
+    from unifiedkv_b200.offload import AsyncOffloadManager
+    from unifiedkv_b200.page16_native import page16_decode_attention
+    from unifiedkv_b200.pool import PagedKVPool, block_table_tensor
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    layers = 1 if getattr(args, "profile_small", False) else LAYERS
+    rng = np.random.default_rng(77)
+    lognorm = lambda n: np.clip(np.exp(rng.normal(np.log(4000), 0.8, size=n)), 256, 32768).astype(np.int64)
+    n_dec, n_pf, chunk = 56, 8, 512
+    dec_len = lognorm(n_dec)
+    pf_past = lognorm(n_pf)
+    total = torch.cuda.get_device_properties(dev).total_memory
+    page_bytes = 2 * layers * 16 * HKV * D * 2
+    pool = PagedKVPool(16, layers, HKV, D, torch.bfloat16, device=dev, n_total=int(0.40 * total) // page_bytes)
+    pool.k_cache.normal_(0, 0.5)
+    pool.v_cache.normal_(0, 0.5)
+    # cold requests: extra decode-length requests worth 20% of the decode pages, held on the host
+    dec_pages = int(np.sum((dec_len + 15) // 16))
+    cold_len = []
+    while sum((l + 15) // 16 for l in cold_len) < 0.2 * dec_pages:
+        cold_len.append(int(lognorm(1)[0]))
+    mgr = AsyncOffloadManager(pool, layers, host_slots=int(0.5 * dec_pages) + 64, staging_pages=512)
+    lens = {}
+    for sid, l in enumerate(list(dec_len) + cold_len):
+        ids = pool.allocate_blocks(int((l + 15) // 16))
+        mgr.register_sequence(sid, ids, int(l))
+        lens[sid] = int(l)
+    active = list(range(n_dec))
+    cold = list(range(n_dec, n_dec + len(cold_len)))
+    for sid in cold:
+        mgr.offload_sequence(sid)
+        mgr._try_finalize_offload(sid, force_sync=True)
+    pf_ids = []
+    for l in pf_past:
+        pf_ids.append(pool.allocate_blocks(int((l + chunk + 15) // 16)))
+    pf_bt = block_table_tensor(pf_ids, dev)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum([chunk] * n_pf)]), dtype=torch.int32, device=dev)
+    sk = torch.tensor(pf_past + chunk, dtype=torch.int32, device=dev)
+    qd = [(torch.randn(n_dec, HQ, D, device=dev) * 0.5).to(torch.bfloat16) for _ in range(layers)]
+    qp = [(torch.randn(n_pf * chunk, HQ, D, device=dev) * 0.5).to(torch.bfloat16) for _ in range(layers)]
+    h2d = {"bytes": 0}
+
+    def step():
+        # 1) the request prefetched during the previous step joins; its pages are valid in stream order
+        incoming = cold[0]
+        mgr.ensure_sequence_blocks_on_gpu(incoming)
+        # 2) prefetch the request that joins next step, on the side stream, overlapping this step
+        nxt = cold[1] if len(cold) > 1 else active[0]
+        mgr._try_finalize_offload(nxt, force_sync=True)  # offloaded >= 1 step ago: already complete
+        mgr.prefetch_sequence_blocks(nxt, list(range(len(mgr.page_table[(nxt, 0)].gpu_block_map))))
+        h2d["bytes"] += ((lens[nxt] + 15) // 16) * page_bytes
+        # 3) one active request leaves (offloaded after this step's reads, on the side stream)
+        outgoing = active[0]
+        batch = active[1:] + [incoming]
+        bt = block_table_tensor([mgr.page_table[(sid, 0)].gpu_block_map for sid in batch], dev)
+        ln = torch.tensor([lens[sid] for sid in batch], dtype=torch.int32).to(dev, non_blocking=True)
+        for l in range(layers):
+            page16_decode_attention(qd[l], pool.k_cache[l], pool.v_cache[l], bt, ln, softmax_scale=D ** -0.5,
+                                    n_rep=HQ // HKV)
+            paged_chunk_prefill(qp[l], pool.k_cache[l], pool.v_cache[l], pf_bt, None, None, D ** -0.5, HQ // HKV,
+                                cu_seqlens_q=cu, seqlens_k=sk, max_seqlen_q=chunk)
+        mgr.offload_sequence(outgoing)
+        active[:] = batch
+        cold.pop(0)
+        cold.append(outgoing)
+        mgr._try_finalize_offload(outgoing, force_sync=False)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    for sid in list(cold):
+        mgr._try_finalize_offload(sid, force_sync=True)
+    h2d["bytes"] = 0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    torch.cuda.current_stream(dev).wait_stream(mgr.transfer_stream)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    toks = n_dec + n_pf * chunk
+    print(json.dumps({
+        "metric": "mixed continuous-batching step tokens/s (config 5)", "value": round(toks / (ms * 1e-3), 1),
+        "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded lengths, N(0,0.5) K/V)",
+        "config": {"workload": "56 decode (lognormal ctx) + 8 x 512-token chunked prefill, 32 layers, pool 40% HBM, "
+                               "20% of decode pages cold in pinned host, one request prefetched + one offloaded per "
+                               "step on the side stream (prefetch issued a step ahead)", "layers": layers, "cold_requests": len(cold_len),
+                   "decode_ctx_mean": float(np.mean(dec_len)), "prefill_past_mean": float(np.mean(pf_past))},
+        "h2d_gb_per_step": round(h2d["bytes"] / args.steps / 1e9, 3),
+        "offload_stats": mgr.get_stats(),
+    }), flush=True)
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "compress", "longseq"],
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "compress", "longseq", "mixed"],
                     help="decode = headline config 2; the others print their own metric line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-small", action="store_true",
@@ -581,7 +690,7 @@ def main():
         elif args.workload == "longseq":
             run_longseq(args, rank, world, local_rank)
         elif rank == 0:
-            run_prefill(args) if args.workload == "prefill" else run_compress(args)
+            {"prefill": run_prefill, "compress": run_compress, "mixed": run_mixed}[args.workload](args)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -153,17 +153,23 @@ __global__ void __launch_bounds__(256, 1) score_stats_tc_kernel(ScoreTcParams p)
       float sv[kTok];
 #pragma unroll
       for (int c0 = 0; c0 < kTok; c0 += 32) tc::tmem_ld32(tcol + c0, sv + c0);
-      // scale > 0: the max of the scaled row is the scaled max of the raw row
+      // scale > 0: the max of the scaled row is the scaled max of the raw row.
+      // Four independent max / sum chains; only the last tile needs the bound.
       const int nvalid = min(kTok, p.Tm - tb);
-      float mx = -INFINITY;
+      if (nvalid < kTok) {
 #pragma unroll
-      for (int c = 0; c < kTok; ++c)
-        if (c < nvalid) mx = fmaxf(mx, sv[c]);
+        for (int c = 0; c < kTok; ++c)
+          if (c >= nvalid) sv[c] = -INFINITY;
+      }
+      float mx4[4] = {sv[0], sv[1], sv[2], sv[3]};
+#pragma unroll
+      for (int c = 4; c < kTok; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sv[c]);
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       const float mn = fmaxf(m, mx * p.scale_log2);
-      float sum = 0.f;
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < kTok; ++c)
-        if (c < nvalid) sum += fast_exp2(fmaf(sv[c], p.scale_log2, -mn));
+      for (int c = 0; c < kTok; ++c) s4[c & 3] += fast_exp2(fmaf(sv[c], p.scale_log2, -mn));
+      const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       l = l * fast_exp2(m - mn) + sum;
       m = mn;
     }
@@ -253,8 +259,10 @@ __global__ void __launch_bounds__(128, 2) score_tokens_tc_kernel(ScoreTcParams p
         const int c0 = r * p.Wp + i0;
         float sv[16];
         tc::tmem_ld16(base + c0, sv);
+        float c4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent chains, then a fixed-order add
 #pragma unroll
-        for (int i = 0; i < 16; ++i) cur += fast_exp2(fmaf(sv[i], p.scale_log2, -s_off[c0 + i]));
+        for (int i = 0; i < 16; ++i) c4[i & 3] += fast_exp2(fmaf(sv[i], p.scale_log2, -s_off[c0 + i]));
+        cur += (c4[0] + c4[1]) + (c4[2] + c4[3]);
       }
       best = fmaxf(best, cur * invW);
     }

@@ -503,16 +503,18 @@ __global__ void __launch_bounds__(kCombWarps * 32) page16_decode_combine_kernel(
   __shared__ int s_slot[kMaxSlotsPerReq];
   __shared__ float s_w[kMaxSlotsPerReq];
   __shared__ float s_red[kCombWarps];
-  __shared__ float s_acc[kCombWarps][256];
+  __shared__ float s_acc[kCombWarps][32];
   __shared__ int s_n;
   const int b = blockIdx.x, hq = blockIdx.y;
+  const int d0 = blockIdx.z * 32;  // this CTA's 32 head_dim columns
   const int64_t T_ = p.g_prefix[p.B];
   const int64_t first = p.g_prefix[b], last = p.g_prefix[b + 1];
   const int D = p.D;
+  if (d0 >= D) return;
   T* ob = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.Hq + hq) * D;
-  float* lse_dst = p.lse_out ? p.lse_out + static_cast<int64_t>(b) * p.Hq + hq : nullptr;
+  float* lse_dst = (p.lse_out && blockIdx.z == 0) ? p.lse_out + static_cast<int64_t>(b) * p.Hq + hq : nullptr;
   if (last == first) {
-    for (int d = threadIdx.x; d < D; d += blockDim.x) ob[d] = Elem<T>::from_f(__int_as_float(0x7fc00000));
+    for (int d = d0 + threadIdx.x; d < min(D, d0 + 32); d += blockDim.x) ob[d] = Elem<T>::from_f(__int_as_float(0x7fc00000));
     if (lse_dst != nullptr && threadIdx.x == 0) *lse_dst = -INFINITY;
     return;
   }
@@ -552,30 +554,20 @@ __global__ void __launch_bounds__(kCombWarps * 32) page16_decode_combine_kernel(
   __syncthreads();
   W = 0.f;
   for (int w = 0; w < kCombWarps; ++w) W += s_red[w];
-  // warp-strided accumulation over parts; lanes cover head_dim (<= 256)
-  float acc[8];
-#pragma unroll
-  for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-#pragma unroll 4
+  // warp-strided accumulation over parts; lane = head_dim column d0 + lane
+  const int d = d0 + lane;
+  float acc = 0.f;
+#pragma unroll 8
   for (int i = warp; i < n; i += kCombWarps) {
-    const float w = s_w[i];
     const float* po = p.part_o + (static_cast<int64_t>(slot(i)) * p.Hq + hq) * D;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int d = lane + 32 * k;
-      if (d < D) acc[k] += w * po[d];
-    }
+    if (d < D) acc += s_w[i] * po[d];
   }
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int d = lane + 32 * k;
-    if (d < D) s_acc[warp][d] = acc[k];
-  }
+  s_acc[warp][lane] = acc;
   __syncthreads();
   const float inv = 1.f / W;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+  if (threadIdx.x < 32 && d < D) {
     float a = 0.f;
-    for (int w = 0; w < kCombWarps; ++w) a += s_acc[w][d];
+    for (int w = 0; w < kCombWarps; ++w) a += s_acc[w][threadIdx.x];
     ob[d] = Elem<T>::from_f(a * inv);
   }
   if (lse_dst != nullptr && threadIdx.x == 0) *lse_dst = M + logf(W);
@@ -659,7 +651,7 @@ int launch_mma(DecodeParams& p, cudaStream_t st) {
     return BPKV_ERR_CUDA;
   }
   kern<<<dim3(G, groups), NW * 32, smem, st>>>(p);
-  page16_decode_combine_kernel<T><<<dim3(p.B, p.Hq), kCombWarps * 32, 0, st>>>(p, G);
+  page16_decode_combine_kernel<T><<<dim3(p.B, p.Hq, (p.D + 31) / 32), kCombWarps * 32, 0, st>>>(p, G);
   BPKV_RETURN_LAUNCH("page16_native_launch");
 }
 
@@ -675,7 +667,7 @@ int launch_generic(DecodeParams& p, cudaStream_t st) {
     return BPKV_ERR_CUDA;
   }
   kern<<<G, NW * 32, smem, st>>>(p);
-  page16_decode_combine_kernel<T><<<dim3(p.B, p.Hq), kCombWarps * 32, 0, st>>>(p, G);
+  page16_decode_combine_kernel<T><<<dim3(p.B, p.Hq, (p.D + 31) / 32), kCombWarps * 32, 0, st>>>(p, G);
   BPKV_RETURN_LAUNCH("page16_native_launch");
 }
 

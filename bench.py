@@ -607,6 +607,9 @@ def run_mixed(args):
     sk = torch.tensor(pf_past + chunk, dtype=torch.int32, device=dev)
     qd = [(torch.randn(n_dec, HQ, D, device=dev) * 0.5).to(torch.bfloat16) for _ in range(layers)]
     qp = [(torch.randn(n_pf * chunk, HQ, D, device=dev) * 0.5).to(torch.bfloat16) for _ in range(layers)]
+    # this step's decode-token K/V rows, stored into the pool by the decode launch itself
+    kd = [(torch.randn(n_dec, HKV, D, device=dev) * 0.5).to(torch.bfloat16) for _ in range(layers)]
+    vd = [(torch.randn(n_dec, HKV, D, device=dev) * 0.5).to(torch.bfloat16) for _ in range(layers)]
     h2d = {"bytes": 0}
 
     def step():
@@ -625,7 +628,7 @@ def run_mixed(args):
         ln = torch.tensor([lens[sid] for sid in batch], dtype=torch.int32).to(dev, non_blocking=True)
         for l in range(layers):
             page16_decode_attention(qd[l], pool.k_cache[l], pool.v_cache[l], bt, ln, softmax_scale=D ** -0.5,
-                                    n_rep=HQ // HKV)
+                                    n_rep=HQ // HKV, k_new=kd[l], v_new=vd[l])
             paged_chunk_prefill(qp[l], pool.k_cache[l], pool.v_cache[l], pf_bt, None, None, D ** -0.5, HQ // HKV,
                                 cu_seqlens_q=cu, seqlens_k=sk, max_seqlen_q=chunk)
         mgr.offload_sequence(outgoing)
@@ -655,7 +658,8 @@ def run_mixed(args):
         "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded lengths, N(0,0.5) K/V)",
         "config": {"workload": "56 decode (lognormal ctx) + 8 x 512-token chunked prefill, 32 layers, pool 40% HBM, "
                                "20% of decode pages cold in pinned host, one request prefetched + one offloaded per "
-                               "step on the side stream (prefetch issued a step ahead)", "layers": layers, "cold_requests": len(cold_len),
+                               "step on the side stream (prefetch issued a step ahead); decode-token K/V appended "
+                               "inside the decode launch", "layers": layers, "cold_requests": len(cold_len),
                    "decode_ctx_mean": float(np.mean(dec_len)), "prefill_past_mean": float(np.mean(pf_past))},
         "h2d_gb_per_step": round(h2d["bytes"] / args.steps / 1e9, 3),
         "offload_stats": mgr.get_stats(),

@@ -87,6 +87,27 @@ BPKV_API int bpkv_page16_decode(const void* q, const void* k_cache, const void* 
                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ *
+ * Page16 decode with the decode-token append fused in.
+ * Replaces the pair "scatter the new k/v into the pool page, then
+ * page16_decode_attention" of direct_forward (core/scheduler.py:398-418).
+ * cache_seqlens include the new token (the reference passes lens+1); the new
+ * token's row k_new/v_new[b] ([batch, num_kv_heads, head_dim], row stride
+ * new_stride_b) is written to the pool at (block_table[b, (len-1)/16],
+ * (len-1) % 16) and used by the same launch.  Requests whose length exceeds
+ * 16*max_blocks are decoded without the append.  Other arguments as
+ * bpkv_page16_decode.
+ * ------------------------------------------------------------------------ */
+BPKV_API int bpkv_page16_decode_append(const void* q, const void* k_new, const void* v_new,
+                       int64_t new_stride_b, void* k_cache, void* v_cache,
+                       const int32_t* block_table, const int32_t* cache_seqlens,
+                       void* out, float* lse_out,
+                       int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                       int max_blocks, int64_t q_stride_b, int64_t q_stride_h,
+                       int64_t page_stride, int64_t bt_stride_b,
+                       float softmax_scale, int dtype,
+                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ *
  * Allocation-free Page16 decode.  No counterpart in the reference: this entry
  * point exists for callers of this library that cannot allocate device memory
  * when they decode - an engine that reserved nearly all of HBM for the paged

@@ -175,6 +175,43 @@ def test_decode_append_then_decode(cuda):
         assert torch.equal(tk[page, l % 16], knew[b]) and torch.equal(tv[page, l % 16], vnew[b])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("d", [64, 128, 256])
+def test_fused_append_matches_append_then_decode(cuda, dtype, d):
+    """The append fused into the decode launch gives bit-identical outputs and pool
+    contents to decode_append followed by page16_decode_attention (lengths that
+    end on a page boundary, a 1-token request, an empty one, one past the
+    block-table capacity, and long ones split across CTAs)."""
+    from unifiedkv_b200.page16_native import decode_append, page16_decode_attention
+    lens = (1, 16, 17, 0, 70, 2000, 4096)
+    hq, hkv, max_blocks = 8, 2, 256
+    q, k, v, bt, lens = page16_case(seed=41 + d, batch=len(lens), hq=hq, hkv=hkv, d=d, lens=lens,
+                                    num_pages=2048, max_blocks=max_blocks, scale_std=0.5)
+    lens = lens.copy()
+    lens[-1] = max_blocks * 16 + 5  # beyond the table: decoded capped, nothing appended
+    g = torch.Generator(device="cpu").manual_seed(7)
+    knew = torch.randn(len(lens), hkv, d, generator=g).to(cuda, dtype)
+    vnew = torch.randn(len(lens), hkv, d, generator=g).to(cuda, dtype)
+    tq = torch.from_numpy(q).to(cuda, dtype)
+    tbt = torch.from_numpy(bt).to(cuda)
+    tl = torch.from_numpy(lens).to(cuda)
+    k0 = torch.from_numpy(k).to(cuda, dtype)
+    v0 = torch.from_numpy(v).to(cuda, dtype)
+    ka, va = k0.clone(), v0.clone()
+    decode_append(knew, vnew, ka, va, tbt, (tl - 1).clamp(min=-1))
+    lse_a = torch.empty(len(lens), hq, device=cuda)
+    out_a = page16_decode_attention(tq, ka, va, tbt, tl, softmax_scale=d ** -0.5, n_rep=hq // hkv, lse_out=lse_a)
+    kf, vf = k0.clone(), v0.clone()
+    lse_f = torch.empty(len(lens), hq, device=cuda)
+    out_f = page16_decode_attention(tq, kf, vf, tbt, tl, softmax_scale=d ** -0.5, n_rep=hq // hkv,
+                                    lse_out=lse_f, k_new=knew, v_new=vnew)
+    torch.cuda.synchronize()
+    assert torch.equal(kf, ka) and torch.equal(vf, va)
+    # the empty request's row is NaN on both paths (0/0, as in the reference)
+    torch.testing.assert_close(out_f, out_a, rtol=0, atol=0, equal_nan=True)
+    torch.testing.assert_close(lse_f, lse_a, rtol=0, atol=0, equal_nan=True)
+
+
 def test_shape_errors_use_reference_tokens(cuda):
     from unifiedkv_b200.page16_native import page16_decode_attention
     q = torch.zeros(2, 6, 64, device=cuda, dtype=torch.bfloat16)

@@ -34,6 +34,9 @@ SIGNATURES = {
                                     _c_int, _c_int, _c_int, _c_int, _c_int,
                                     _c_i64, _c_i64, _c_i64, _c_i64, _c_f, _c_int,
                                     _c_p, _c_sz, _c_p]),
+    "bpkv_page16_decode_append": (_c_int, [_c_p, _c_p, _c_p, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+                                           _c_int, _c_int, _c_int, _c_int, _c_int,
+                                           _c_i64, _c_i64, _c_i64, _c_i64, _c_f, _c_int, _c_p, _c_sz, _c_p]),
     "bpkv_page16_decode_noalloc_max_scratch": (_c_sz, []),
     "bpkv_page16_decode_noalloc": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
                                             _c_int, _c_int, _c_int, _c_int, _c_int,

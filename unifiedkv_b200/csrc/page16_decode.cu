@@ -44,6 +44,10 @@ struct DecodeParams {
   int64_t q_sb, q_sh, page_stride, bt_sb;
   float scale;        // softmax scale
   float scale_log2;   // softmax scale * log2(e)
+  // fused decode-token append (null = off): row [batch][h_kv][d] written at token len-1
+  const void* k_new;
+  const void* v_new;
+  int64_t new_sb;
 };
 
 constexpr float kLn2 = 0.6931471805599453f;
@@ -148,7 +152,12 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
   auto issue = [&](int64_t fp, int b, int stage) {
     const int j = static_cast<int>(fp - prefix[b]);
     const int page = __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + j);
-    const int valid_rows = eff_len(p, b) - j * kPage;  // >= 1
+    const int len_b = eff_len(p, b);
+    const int valid_rows = len_b - j * kPage;  // >= 1
+    // fused append: this step's token (position len-1) lives in the request's last page; its row
+    // comes from k_new / v_new and is also stored to the pool page (no other CTA reads that page)
+    const bool last_page = j == prefix[b + 1] - prefix[b] - 1;
+    const int tok_new = (p.k_new != nullptr && last_page && __ldg(p.lens + b) == len_b) ? valid_rows - 1 : -1;
     const int64_t base = static_cast<int64_t>(page) * p.page_stride + static_cast<int64_t>(h) * D;
     const uint32_t sk = ring + stage * STAGEB;
     const uint32_t sv = sk + TILEB;
@@ -159,6 +168,16 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
       const bool ok = tok < valid_rows;
       const int64_t off = base + static_cast<int64_t>(tok) * p.Hkv * D + ch * 8;
       const uint32_t so = tok * ROWB + ((ch ^ (tok & 7)) << 4);
+      if (tok == tok_new) {
+        const int64_t noff = static_cast<int64_t>(b) * p.new_sb + static_cast<int64_t>(h) * D + ch * 8;
+        const T* kn = reinterpret_cast<const T*>(p.k_new) + noff;
+        const T* vn = reinterpret_cast<const T*>(p.v_new) + noff;
+        cp_async16(sk + so, kn, true);
+        cp_async16(sv + so, vn, true);
+        *reinterpret_cast<uint4*>(static_cast<T*>(const_cast<void*>(p.k)) + off) = *reinterpret_cast<const uint4*>(kn);
+        *reinterpret_cast<uint4*>(static_cast<T*>(const_cast<void*>(p.v)) + off) = *reinterpret_cast<const uint4*>(vn);
+        continue;
+      }
       cp_async16(sk + so, ok ? (const void*)(kg + off) : (const void*)kg, ok);
       cp_async16(sv + so, ok ? (const void*)(vg + off) : (const void*)vg, ok);
     }
@@ -586,6 +605,24 @@ __global__ void lse_combine_kernel(const float* part_o, const float* part_lse, v
 
 // ---------------------------------------------------------------------------
 // Decode-token append.
+
+// Append for the generic decode path: the new token goes to position len-1 (lengths include it).
+template <typename T>
+__global__ void decode_append_len_kernel(DecodeParams p) {
+  const int b = blockIdx.x;
+  const int len = p.lens[b];
+  if (len <= 0 || len > p.max_blocks * kPage) return;
+  const int pos = len - 1;
+  const int page = p.bt[static_cast<int64_t>(b) * p.bt_sb + pos / kPage];
+  const int64_t dst = static_cast<int64_t>(page) * p.page_stride + static_cast<int64_t>(pos % kPage) * p.Hkv * p.D;
+  const int64_t src = static_cast<int64_t>(b) * p.new_sb;
+  T* kc = const_cast<T*>(reinterpret_cast<const T*>(p.k));
+  T* vc = const_cast<T*>(reinterpret_cast<const T*>(p.v));
+  for (int i = threadIdx.x; i < p.Hkv * p.D; i += blockDim.x) {
+    kc[dst + i] = reinterpret_cast<const T*>(p.k_new)[src + i];
+    vc[dst + i] = reinterpret_cast<const T*>(p.v_new)[src + i];
+  }
+}
 // ---------------------------------------------------------------------------
 template <typename T>
 __global__ void decode_append_kernel(const T* k_new, const T* v_new, T* k_cache, T* v_cache,
@@ -656,8 +693,17 @@ int launch_mma(DecodeParams& p, cudaStream_t st) {
 }
 
 template <typename T>
+__global__ void decode_append_kernel(const T* k_new, const T* v_new, T* k_cache, T* v_cache,
+                                     const int32_t* bt, const int32_t* old_lens, int Hkv, int D,
+                                     int max_blocks, int64_t new_sb, int64_t page_stride,
+                                     int64_t bt_sb);
+template <typename T>
+__global__ void decode_append_len_kernel(DecodeParams p);
+
+template <typename T>
 int launch_generic(DecodeParams& p, cudaStream_t st) {
   constexpr int NW = 8;
+  if (p.k_new != nullptr) decode_append_len_kernel<T><<<p.B, 256, 0, st>>>(p);  // append, then decode
   const int G = sm_count();
   const size_t smem = sizeof(int) * (p.B + 1);
   auto kern = page16_decode_generic_kernel<T, NW>;
@@ -696,13 +742,13 @@ extern "C" BPKV_API size_t bpkv_page16_decode_workspace_size(int batch, int num_
   return ws_layout(batch, num_q_heads, head_dim).total;
 }
 
-extern "C" BPKV_API int bpkv_page16_decode(const void* q, const void* k_cache, const void* v_cache,
-                                  const int32_t* block_table, const int32_t* cache_seqlens,
-                                  void* out, float* lse_out, int batch, int num_q_heads,
-                                  int num_kv_heads, int head_dim, int max_blocks,
-                                  int64_t q_stride_b, int64_t q_stride_h, int64_t page_stride,
-                                  int64_t bt_stride_b, float softmax_scale, int dtype,
-                                  void* workspace, size_t workspace_bytes, void* stream) {
+static int page16_decode_impl(const void* q, const void* k_cache, const void* v_cache,
+                              const int32_t* block_table, const int32_t* cache_seqlens, void* out,
+                              float* lse_out, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                              int max_blocks, int64_t q_stride_b, int64_t q_stride_h, int64_t page_stride,
+                              int64_t bt_stride_b, float softmax_scale, int dtype, void* workspace,
+                              size_t workspace_bytes, void* stream, const void* k_new, const void* v_new,
+                              int64_t new_stride_b) {
   clear_error();
   BPKV_CHECK_ARG(batch > 0 && num_q_heads > 0 && head_dim > 0, "page16_native_shape_unsupported:empty");
   BPKV_CHECK_ARG(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "page16_native_shape_unsupported:gqa");
@@ -742,15 +788,48 @@ extern "C" BPKV_API int bpkv_page16_decode(const void* q, const void* k_cache, c
   p.bt_sb = bt_stride_b;
   p.scale = softmax_scale;
   p.scale_log2 = softmax_scale * 1.4426950408889634f;
+  p.k_new = k_new;
+  p.v_new = v_new;
+  p.new_sb = new_stride_b;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   const bool fast_ok = dtype != BPKV_F32 && (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
                        p.n_rep <= 16 && batch <= 4096 && aligned16(q) && aligned16(k_cache) &&
                        aligned16(v_cache) && aligned16(out) && (q_stride_b % 8 == 0) &&
-                       (q_stride_h % 8 == 0) && (page_stride % 8 == 0);
+                       (q_stride_h % 8 == 0) && (page_stride % 8 == 0) &&
+                       (k_new == nullptr || (aligned16(k_new) && aligned16(v_new) && new_stride_b % 8 == 0));
   if (dtype == BPKV_BF16) return dispatch<__nv_bfloat16>(p, st, fast_ok);
   if (dtype == BPKV_F16) return dispatch<__half>(p, st, fast_ok);
   return dispatch<float>(p, st, false);
+}
+
+extern "C" BPKV_API int bpkv_page16_decode(const void* q, const void* k_cache, const void* v_cache,
+                                           const int32_t* block_table, const int32_t* cache_seqlens, void* out,
+                                           float* lse_out, int batch, int num_q_heads, int num_kv_heads,
+                                           int head_dim, int max_blocks, int64_t q_stride_b, int64_t q_stride_h,
+                                           int64_t page_stride, int64_t bt_stride_b, float softmax_scale, int dtype,
+                                           void* workspace, size_t workspace_bytes, void* stream) {
+  return page16_decode_impl(q, k_cache, v_cache, block_table, cache_seqlens, out, lse_out, batch, num_q_heads,
+                            num_kv_heads, head_dim, max_blocks, q_stride_b, q_stride_h, page_stride, bt_stride_b,
+                            softmax_scale, dtype, workspace, workspace_bytes, stream, nullptr, nullptr, 0);
+}
+
+extern "C" BPKV_API int bpkv_page16_decode_append(const void* q, const void* k_new, const void* v_new,
+                                                  int64_t new_stride_b, void* k_cache, void* v_cache,
+                                                  const int32_t* block_table, const int32_t* cache_seqlens,
+                                                  void* out, float* lse_out, int batch, int num_q_heads,
+                                                  int num_kv_heads, int head_dim, int max_blocks, int64_t q_stride_b,
+                                                  int64_t q_stride_h, int64_t page_stride, int64_t bt_stride_b,
+                                                  float softmax_scale, int dtype, void* workspace,
+                                                  size_t workspace_bytes, void* stream) {
+  if (k_new == nullptr || v_new == nullptr) {
+    clear_error();
+    set_error("page16_native_shape_unsupported:null_new_token");
+    return BPKV_ERR_SHAPE;
+  }
+  return page16_decode_impl(q, k_cache, v_cache, block_table, cache_seqlens, out, lse_out, batch, num_q_heads,
+                            num_kv_heads, head_dim, max_blocks, q_stride_b, q_stride_h, page_stride, bt_stride_b,
+                            softmax_scale, dtype, workspace, workspace_bytes, stream, k_new, v_new, new_stride_b);
 }
 
 extern "C" BPKV_API int bpkv_lse_combine(const float* part_out, const float* part_lse, void* out,

@@ -64,6 +64,8 @@ def page16_decode_attention(
     softmax_scale: float,
     n_rep: int,
     lse_out: torch.Tensor | None = None,
+    k_new: torch.Tensor | None = None,
+    v_new: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Decode-only paged attention over 16-token pages (sm_100a split-KV kernel).
 
@@ -80,6 +82,12 @@ def page16_decode_attention(
     ``lse_out`` (optional, this build's addition): fp32 [batch, num_q_heads]
     receives the natural-log sum-exp of the scaled logits, used to merge
     split-KV partials across GPUs.
+
+    ``k_new``/``v_new`` (optional, this build's addition): [batch, num_kv_heads,
+    head_dim] rows of this step's token.  The launch stores them into the pool
+    at position ``cache_seqlens[b] - 1`` and attends over them in the same pass,
+    replacing the scatter-then-attend pair of direct_forward
+    (core/scheduler.py:398-418).
     """
     batch, num_q_heads, num_kv_heads, head_dim = _check_shapes(q, k_cache, v_cache, block_table, cache_seqlens)
     if int(n_rep) != num_q_heads // num_kv_heads:
@@ -102,22 +110,42 @@ def page16_decode_attention(
     if lse_out is not None:
         if lse_out.dtype != torch.float32 or lse_out.numel() != batch * num_q_heads or not lse_out.is_contiguous():
             raise RuntimeError("page16_native_shape_unsupported:lse_out")
+    if (k_new is None) != (v_new is None):
+        raise RuntimeError("page16_native_shape_unsupported:new_token")
+    if k_new is not None:
+        want = (batch, num_kv_heads, head_dim)
+        if tuple(k_new.shape) != want or tuple(v_new.shape) != want:
+            raise RuntimeError("page16_native_shape_unsupported:new_token")
+        if k_new.dtype != q.dtype or v_new.dtype != q.dtype or not (k_new.is_cuda and v_new.is_cuda):
+            raise RuntimeError("page16_native_shape_unsupported:new_token")
+        k_new = k_new.contiguous()
+        v_new = v_new.contiguous()
     dev = q.device
     if dev.index != torch.cuda.current_device():  # the library launches on the current device
         with torch.cuda.device(dev):
             return page16_decode_attention(q, k_cache, v_cache, block_table, cache_seqlens,
-                                           softmax_scale=softmax_scale, n_rep=n_rep, lse_out=lse_out)
+                                           softmax_scale=softmax_scale, n_rep=n_rep, lse_out=lse_out,
+                                           k_new=k_new, v_new=v_new)
     L = _lib.lib()
     code = _lib.dtype_code(q.dtype)
     stream = torch.cuda.current_stream(dev)
     ws = _lib.workspace_for(L.bpkv_page16_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, code),
                             dev, stream, "page16")
-    rc = L.bpkv_page16_decode(
-        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
-        cache_seqlens.data_ptr(), out.data_ptr(), _lib.ptr(lse_out),
-        batch, num_q_heads, num_kv_heads, head_dim, int(block_table.shape[1]),
-        q.stride(0), q.stride(1), k_cache.stride(0), block_table.stride(0),
-        float(softmax_scale), code, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+    if k_new is None:
+        rc = L.bpkv_page16_decode(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
+            cache_seqlens.data_ptr(), out.data_ptr(), _lib.ptr(lse_out),
+            batch, num_q_heads, num_kv_heads, head_dim, int(block_table.shape[1]),
+            q.stride(0), q.stride(1), k_cache.stride(0), block_table.stride(0),
+            float(softmax_scale), code, ws.data_ptr(), ws.numel(), stream.cuda_stream)
+    else:
+        rc = L.bpkv_page16_decode_append(
+            q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0),
+            k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(),
+            cache_seqlens.data_ptr(), out.data_ptr(), _lib.ptr(lse_out),
+            batch, num_q_heads, num_kv_heads, head_dim, int(block_table.shape[1]),
+            q.stride(0), q.stride(1), k_cache.stride(0), block_table.stride(0),
+            float(softmax_scale), code, ws.data_ptr(), ws.numel(), stream.cuda_stream)
     _lib.check(rc, "page16_native")
     return out
 

@@ -109,6 +109,20 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
+constexpr int kMaxRanked = 512;  // q-tile items ranked per CTA (n^2 / kThreads compares)
+
+// K/V tiles a (request, q-tile) item iterates over (-1: item past the request's queries)
+__device__ __forceinline__ int item_tiles(const PrefillTcParams& p, int i) {
+  const int b = i / p.tiles_per_req, qt = i % p.tiles_per_req;
+  const int q0 = __ldg(p.cu_q + b), nq = __ldg(p.cu_q + b + 1) - q0;
+  const int tq = kBM / p.n_rep, tok0 = qt * tq;
+  if (tok0 >= nq) return -1;
+  const int sk = p.seqlens_k != nullptr ? __ldg(p.seqlens_k + b) : nq;
+  const int last_tok = min(tok0 + tq, nq) - 1;
+  const int kv_end = p.causal ? min(sk, sk - nq + last_tok + 1) : sk;
+  return kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
+}
+
 template <typename T, bool PAGED>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ TcKernelArgs args) {
   const PrefillTcParams& p = args.p;
@@ -124,16 +138,40 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   float* s_mx = reinterpret_cast<float*>(s_pages + kMaxPagesSmem);  // [2 buffers][kSplit parts][kBM]
   float* s_l = s_mx + 2 * kSplit * kBM;                                // [kSplit parts][kBM]
 
-  const int b = blockIdx.x / p.tiles_per_req;
-  const int qt = blockIdx.x % p.tiles_per_req;
-  const int hkv = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // ---- work item of this CTA: longest first ----
+  // CTA c takes (q-tile item of rank c / Hkv, kv head c % Hkv), items ranked by
+  // their number of K/V tiles, descending (ties: lower index first), so the
+  // long causal tiles of long requests start in the first wave instead of
+  // forming the tail.  Beyond kMaxRanked items the natural order is kept.
+  const int n_items = p.B * p.tiles_per_req;
+  const int hkv = static_cast<int>(blockIdx.x % p.Hkv);
+  int item = static_cast<int>(blockIdx.x / p.Hkv);
+  if (n_items <= kMaxRanked) {
+    int* s_work = reinterpret_cast<int*>(bars + 32);  // the block-table staging area, not yet in use
+    __shared__ int s_item;
+    for (int i = tid; i < n_items; i += kThreads) s_work[i] = item_tiles(p, i);
+    __syncthreads();
+    for (int i = tid; i < n_items; i += kThreads) {
+      const int wi = s_work[i];
+      int rank = 0;
+      for (int j = 0; j < n_items; ++j) {
+        const int wj = s_work[j];
+        rank += (wj > wi) || (wj == wi && j < i);
+      }
+      if (rank == item) s_item = i;
+    }
+    __syncthreads();
+    item = s_item;
+  }
+  const int b = item / p.tiles_per_req;
+  const int qt = item % p.tiles_per_req;
   const int q0 = p.cu_q[b];
   const int nq = p.cu_q[b + 1] - q0;
   const int TQ = kBM / p.n_rep;
   const int tok0 = qt * TQ;
   if (tok0 >= nq) return;  // uniform across the CTA: before any barrier or TMEM use
   const int sk = PAGED ? p.seqlens_k[b] : nq;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const T* qg = reinterpret_cast<const T*>(p.q);
   const T* kg = reinterpret_cast<const T*>(p.k);
   const T* vg = reinterpret_cast<const T*>(p.v);
@@ -559,7 +597,7 @@ int prefill_tc_launch(PrefillTcParams& p, int head_dim, int dtype, int max_seqle
       return BPKV_ERR_CUDA;
     }
   }
-  dim3 grid(p.B * p.tiles_per_req, p.Hkv);
+  dim3 grid(p.B * p.tiles_per_req * p.Hkv);
   static bool raised[4][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);

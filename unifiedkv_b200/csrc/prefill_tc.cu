@@ -53,23 +53,23 @@ __device__ unsigned long long g_prefill_trace[16];
 
 namespace {
 
-constexpr int kD = 128, kBM = 128, kBN = 64, kDB = kD / 64;
+// An M=128 tcgen05.mma costs the same tensor-pipe time for any N <= 128 (measured:
+// ~64 cycles per K=16 step), so K/V tiles are 128 tokens: S = Q K^T runs at N=128.
+constexpr int kD = 128, kBM = 128, kBN = 128, kDB = kD / 64;
 constexpr int kQBytes = kDB * kBM * 128;       // 32 KB
-constexpr int kKVBytes = kDB * kBN * 128;      // 16 KB per K or V tile
-constexpr int kPBytes = kBM * 128;             // 16 KB (64 tokens per row)
-constexpr int kNK = 6;                         // K ring depth (K(j) is free once S(j) completed)
-constexpr int kNV = 5;                         // V ring depth (V(j) is free once PV(j) completed)
-constexpr int kPBufBytes = 2 * kPBytes;        // one P buffer: hi + lo parts
+constexpr int kKVBytes = kDB * kBN * 128;      // 32 KB per K or V tile
+constexpr int kNK = 2;                         // K ring depth (K(j) is free once S(j) completed)
+constexpr int kNV = 3;                         // V ring depth (V(j) is free once PV(j) completed)
 constexpr int kSplit = 4;                      // softmax threads per accumulator row
 constexpr int kSoftmaxWarps = 4 * kSplit;      // warps 0..15: softmax
 constexpr int kLoadWarp = kSoftmaxWarps;       // warp 8: TMA / cp.async loads
 constexpr int kMmaWarp = kSoftmaxWarps + 1;    // warp 9: tcgen05.mma issue
 constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
 constexpr int kMaxPagesSmem = 2048;            // block-table entries staged in shared memory
-constexpr int kSmemBytes = (kNK + kNV) * kKVBytes + 1024 /*align*/ + 256 + 4 * kMaxPagesSmem +
+constexpr int kSmemBytes = kQBytes + (kNK + kNV) * kKVBytes + 1024 /*align*/ + 256 + 4 * kMaxPagesSmem +
                             4 * 2 * kSplit * kBM /*row-max exchange*/ + 4 * kSplit * kBM /*row sums*/;
-constexpr uint32_t kTmemCols = 512;            // S0 [0,64) S1 [64,128) O [128,256) Q [256,320) P [320,448)
-constexpr uint32_t kTmemQ = 256, kTmemP = 320;  // bf16 pairs per 32-bit column
+constexpr uint32_t kTmemCols = 512;            // S0 [0,128) S1 [128,256) O [256,384) P hi [384,448) lo [448,512)
+constexpr uint32_t kTmemO = 256, kTmemP = 384;  // P: bf16 pairs per 32-bit column
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 256 between rescales
 
 struct __align__(64) TcKernelArgs {
@@ -128,7 +128,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   const PrefillTcParams& p = args.p;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ks = smem;                    // kNK buffers
+  uint8_t* qs = smem;                    // Q tile (A operand of S = Q K^T)
+  uint8_t* ks = qs + kQBytes;            // kNK buffers
   uint8_t* vs = ks + kNK * kKVBytes;     // kNV buffers
   uint64_t* bars = reinterpret_cast<uint64_t*>(vs + kNV * kKVBytes);
   // bars: k_full[kNK], v_full[kNV], s_full[2], p_full[2], o_done[2], k_free[kNK], v_free[kNV]
@@ -211,31 +212,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   __syncthreads();  // barriers initialised, TMEM address published, block table staged
   tc::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // ---- Q tile -> TMEM (A operand of S = Q K^T): row m = (token tok0 + m / n_rep, head m % n_rep),
-  //      lane m, 32-bit column k/2 holds q[m][k], q[m][k+1] ----
+  // ---- Q tile -> shared memory, 128-B swizzled K-major: row m = (token tok0 + m / n_rep,
+  //      head m % n_rep); [d-block][row][128 B] ----
   if (warp < 4) {
     const int m = tid;
     const int tq = tok0 + m / p.n_rep, r = m % p.n_rep;
     const uint4* src = reinterpret_cast<const uint4*>(qg + (static_cast<int64_t>(q0 + tq) * p.Hq + hkv * p.n_rep + r) * kD);
-    const uint32_t qlane = static_cast<uint32_t>(warp * 32) << 16;
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t u[32];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint4 v = tq < nq ? __ldg(src + half * 8 + i) : make_uint4(0, 0, 0, 0);
-        u[4 * i] = v.x;
-        u[4 * i + 1] = v.y;
-        u[4 * i + 2] = v.z;
-        u[4 * i + 3] = v.w;
-      }
-      tc::tmem_st32u(tmem + kTmemQ + qlane + half * 32, u);
+    for (int ch = 0; ch < kD / 8; ++ch) {
+      const uint4 v = tq < nq ? __ldg(src + ch) : make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(qs + (ch >> 3) * (kBM * 128) + sw_off(m, ch & 7)) = v;
     }
+    tc::fence_proxy_async_smem();
   }
   tc::tc_fence_before();
-  __syncthreads();  // Q resident in TMEM
+  __syncthreads();  // Q resident in shared memory
   tc::tc_fence_after();
-  const uint32_t t_o = tmem + 2u * kBN;
+  const uint32_t t_o = tmem + kTmemO;
   auto t_s = [&](int j) { return tmem + static_cast<uint32_t>((j & 1) * kBN); };
   constexpr bool kBf16 = SplitP<T>::value;
 
@@ -275,15 +268,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const uint32_t id_o = tc::idesc_f16(kBf16, false, true, kBM, kD);
     // Descriptors are built once; per k-step only the start-address field (bits
     // 0-13, address >> 4) advances, which stays inside the field for smem < 256 KB.
+    const uint64_t dq0 = tc::smem_desc_sw128(smem_u32(qs), 16, 1024);
     const uint64_t dk0 = tc::smem_desc_sw128(smem_u32(ks), 16, 1024);
     const uint64_t dv0 = tc::smem_desc_sw128(smem_u32(vs), kBN * 128, 1024);
-    auto issue_s = [&](int j) {  // S(j) = Q K(j)^T, Q from TMEM
+    auto issue_s = [&](int j) {  // S(j) = Q K(j)^T, both operands from shared memory
       tc::tc_fence_after();
       const uint64_t kb = dk0 + static_cast<uint64_t>(((j % kNK) * kKVBytes) >> 4);
 #pragma unroll
       for (int kk = 0; kk < kD / 16; ++kk) {
+        const uint64_t qoff = static_cast<uint64_t>(((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4);
         const uint64_t kboff = static_cast<uint64_t>(((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4);
-        tc::mma_f16_ts(t_s(j), tmem + kTmemQ + kk * 8, kb + kboff, id_s, kk > 0 ? 1u : 0u);
+        tc::mma_f16(t_s(j), dq0 + qoff, kb + kboff, id_s, kk > 0 ? 1u : 0u);
       }
       tc::mma_commit(s_full(j));
     };
@@ -292,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const uint64_t vb = dv0 + static_cast<uint64_t>(((j % kNV) * kKVBytes) >> 4);
       const int parts = kBf16 ? 2 : 1;
       for (int part = 0; part < parts; ++part) {
-        const uint32_t pa = tmem + kTmemP + (j & 1) * 64 + part * 32;
+        const uint32_t pa = tmem + kTmemP + part * (kBN / 2);
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
           tc::mma_f16_ts(t_o, pa + kk * 8, vb + static_cast<uint64_t>((kk * 16 * 128) >> 4), id_o,
@@ -380,10 +375,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       wait(s_full(it), (it >> 1) & 1);
       tc::tc_fence_after();
       float s[kSC];
+      static_assert(kSC == 32, "one x32 TMEM load per thread and tile");
 #ifdef BPKV_TRACE
       long long _tl = clock64();
 #endif
-      tc::tmem_ld16(t_s(it) + lane_base + sc0, s);
+      tc::tmem_ld32(t_s(it) + lane_base + sc0, s);
 #ifdef BPKV_TRACE
       if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[8], static_cast<unsigned long long>(clock64() - _tl));
       _tl = clock64();
@@ -444,8 +440,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[13], static_cast<unsigned long long>(clock64() - _tl));
       _tl = clock64();
 #endif
-      if (it >= 2) {  // P buffer it&1 was last read by PV(it-2)
-        wait(o_done(it - 2), ((it - 2) >> 1) & 1);
+      if (it >= 1) {  // the P buffer was last read by PV(it-1)
+        wait(o_done(it - 1), ((it - 1) >> 1) & 1);
       }
       const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
@@ -461,11 +457,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[14], static_cast<unsigned long long>(clock64() - _tl));
       _tl = clock64();
 #endif
-      // P(it) -> TMEM buffer it&1: 32-bit column = token pair
-      const uint32_t pcol = tmem + kTmemP + (it & 1) * 64 + lane_base + sc0 / 2;
-      static_assert(kSC / 2 == 8, "one x8 store per part");
-      tc::tmem_st8(pcol, hi);
-      if (kBf16) tc::tmem_st8(pcol + 32, lo);
+      // P(it) -> TMEM: 32-bit column = token pair; hi part, then lo part kBN/2 columns on
+      tc::tc_fence_after();
+      const uint32_t pcol = tmem + kTmemP + lane_base + sc0 / 2;
+      tc::tmem_st16(pcol, hi);
+      if (kBf16) tc::tmem_st16(pcol + kBN / 2, lo);
 #ifdef BPKV_TRACE
       if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[15], static_cast<unsigned long long>(clock64() - _tl));
       _tl = clock64();

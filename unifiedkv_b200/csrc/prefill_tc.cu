@@ -46,9 +46,27 @@ struct PrefillTcParams {
 #ifdef BPKV_TRACE
 // Debug builds only (-DBPKV_TRACE): per-phase clock64 totals of CTA (0,0).
 __device__ unsigned long long g_prefill_trace[16];
-#define BPKV_T0() const long long _t0 = clock64()
-#define BPKV_TADD(slot) atomicAdd(&g_prefill_trace[slot], static_cast<unsigned long long>(clock64() - _t0))
-#define BPKV_TRACING (blockIdx.x == 0 && blockIdx.y == 0)
+#define BPKV_TRACING (blockIdx.x == 0)
+// consecutive checkpoints of thread 0: slot k accumulates the cycles since the previous mark
+#define BPKV_MARK(slot)                                                                          \
+  do {                                                                                           \
+    const long long _n = clock64();                                                              \
+    if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[slot], static_cast<unsigned long long>(_n - _tl)); \
+    _tl = _n;                                                                                    \
+  } while (0)
+#define BPKV_MARK_MMA(slot)                                                                      \
+  do {                                                                                           \
+    const long long _n = clock64();                                                              \
+    if (BPKV_TRACING && lane == 0) atomicAdd(&g_prefill_trace[slot], static_cast<unsigned long long>(_n - _tm)); \
+    _tm = _n;                                                                                    \
+  } while (0)
+#else
+#define BPKV_MARK_MMA(slot) \
+  do {                      \
+  } while (0)
+#define BPKV_MARK(slot) \
+  do {                  \
+  } while (0)
 #endif
 
 namespace {
@@ -58,8 +76,8 @@ namespace {
 constexpr int kD = 128, kBM = 128, kBN = 128, kDB = kD / 64;
 constexpr int kQBytes = kDB * kBM * 128;       // 32 KB
 constexpr int kKVBytes = kDB * kBN * 128;      // 32 KB per K or V tile
-constexpr int kNK = 2;                         // K ring depth (K(j) is free once S(j) completed)
-constexpr int kNV = 3;                         // V ring depth (V(j) is free once PV(j) completed)
+constexpr int kNK = 3;                         // K ring depth (K(j) is free once S(j) completed)
+constexpr int kNV = 2;                         // V ring depth (V(j) is free once PV(j) completed)
 constexpr int kSplit = 4;                      // softmax threads per accumulator row
 constexpr int kSoftmaxWarps = 4 * kSplit;      // warps 0..15: softmax
 constexpr int kLoadWarp = kSoftmaxWarps;       // warp 8: TMA / cp.async loads
@@ -108,6 +126,65 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
       "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
       : "memory");
 }
+
+// ---- packed fp32 pairs (f32x2 arithmetic of sm_100) ----
+__device__ __forceinline__ uint64_t pk2(float a, float b) {  // a -> low half, b -> high half
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void up2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// 2^x of a pair on the FMA pipe instead of the MUFU unit (which issues only 16
+// exponentials per clock per SM and bounds the softmax).  Cody-Waite range
+// reduction x = n + f, n = rint(x) via the 1.5*2^23 rounding constant, f in
+// [-0.5, 0.5]; 2^f by a degree-5 polynomial whose coefficients were fitted by
+// weighted least squares (Lawson iterations towards minimax relative error;
+// max relative error 2.4e-7 evaluated in fp32, comparable to ex2.approx);
+// 2^n is assembled in the exponent field from the low bits of the rounded sum.
+// Valid for x < 128; x <= -127 gives exactly 0 (so -inf, masked, gives 0); NaN gives NaN.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+  float xa, xb;
+  up2(x2, xa, xb);
+  xa = xa < -127.f ? -127.f : xa;  // (a NaN stays NaN)
+  xb = xb < -127.f ? -127.f : xb;
+  const uint64_t x = pk2(xa, xb);
+  const float kRound = 12582912.f + 127.f;  // 1.5*2^23 + exponent bias
+  const uint64_t t = add2(x, pk2(kRound, kRound));
+  const uint64_t f = sub2(x, sub2(t, pk2(kRound, kRound)));
+  uint64_t q = fma2(f, pk2(1.327647129073739e-3f, 1.327647129073739e-3f), pk2(9.675540961325169e-3f, 9.675540961325169e-3f));
+  q = fma2(q, f, pk2(5.550713092088699e-2f, 5.550713092088699e-2f));
+  q = fma2(q, f, pk2(2.4022120237350464e-1f, 2.4022120237350464e-1f));
+  q = fma2(q, f, pk2(6.931469440460205e-1f, 6.931469440460205e-1f));
+  q = fma2(q, f, pk2(1.0000001192092896f, 1.0000001192092896f));
+  float ta, tb;
+  up2(t, ta, tb);
+  const uint64_t scale = pk2(__uint_as_float(__float_as_uint(ta) << 23), __uint_as_float(__float_as_uint(tb) << 23));
+  return mul2(q, scale);
+}
+constexpr int kEmuStride = 8;  // every kEmuStride-th exponential pair goes to the FMA pipe
 
 constexpr int kMaxRanked = 512;  // q-tile items ranked per CTA (n^2 / kThreads compares)
 
@@ -313,29 +390,41 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         __syncwarp();
       }
     } else {
-      if (n_tiles > 0) {
-        ok = tc::mbar_wait(k_full(0), 0);
+      // Tensor-pipe order: S(0) S(1) | PV(0) S(2) | PV(1) S(3) | ...  S(j+2) reuses the S buffer
+      // of S(j), which softmax(j) has read before it published P(j); issuing it right behind
+      // PV(j) (instead of ahead of PV(j-1)) has S ready when the softmax warps finish P(j).
+      for (int j = 0; ok && j < 2 && j < n_tiles; ++j) {
+        ok = tc::mbar_wait(k_full(j), (j / kNK) & 1);
         if (ok && lane == 0) {
-          issue_s(0);
-          tc::mma_commit(k_free(0));
+          issue_s(j);
+          tc::mma_commit(k_free(j));
         }
+        __syncwarp();
       }
+#ifdef BPKV_TRACE
+      long long _tm = clock64();
+#endif
       for (int j = 0; ok && j < n_tiles; ++j) {
-        if (j + 1 < n_tiles) {
-          ok = tc::mbar_wait(k_full(j + 1), ((j + 1) / kNK) & 1);
-          if (!ok) break;
-          if (lane == 0) {
-            issue_s(j + 1);
-            tc::mma_commit(k_free(j + 1));
-          }
-        }
+        BPKV_MARK_MMA(15);
         ok = tc::mbar_wait(p_full(j), (j >> 1) & 1);  // softmax(j) wrote P(j), done with S(j)
         if (!ok) break;
+        BPKV_MARK_MMA(12);
         ok = tc::mbar_wait(v_full(j), (j / kNV) & 1);
         if (!ok) break;
+        BPKV_MARK_MMA(13);
         if (lane == 0) {
           issue_o(j);
           tc::mma_commit(v_free(j));
+        }
+        BPKV_MARK_MMA(9);
+        if (j + 2 < n_tiles) {
+          ok = tc::mbar_wait(k_full(j + 2), ((j + 2) / kNK) & 1);
+          if (!ok) break;
+          BPKV_MARK_MMA(14);
+          if (lane == 0) {
+            issue_s(j + 2);
+            tc::mma_commit(k_free(j + 2));
+          }
         }
         __syncwarp();
       }
@@ -359,31 +448,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     bool failed = false;
     auto wait = [&](uint32_t bar, uint32_t parity) {
       if (failed) return;
-#ifdef BPKV_TRACE
-      BPKV_T0();
-#endif
       const bool r = tc::mbar_wait(bar, parity);
-#ifdef BPKV_TRACE
-      if (BPKV_TRACING && tid == 0) BPKV_TADD(4);
-#endif
       if (!__all_sync(0xffffffffu, r)) failed = true;
     };
 #ifdef BPKV_TRACE
-    const long long _tstart = clock64();
+    long long _tl = clock64();
+    const long long _tstart = _tl;
 #endif
     for (int it = 0; it < n_tiles; ++it) {
       wait(s_full(it), (it >> 1) & 1);
+      BPKV_MARK(0);
       tc::tc_fence_after();
       float s[kSC];
       static_assert(kSC == 32, "one x32 TMEM load per thread and tile");
-#ifdef BPKV_TRACE
-      long long _tl = clock64();
-#endif
       tc::tmem_ld32(t_s(it) + lane_base + sc0, s);
-#ifdef BPKV_TRACE
-      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[8], static_cast<unsigned long long>(clock64() - _tl));
-      _tl = clock64();
-#endif
+      BPKV_MARK(1);
       const int tbase = it * kBN + sc0;
       if (tbase + kSC - 1 > lim) {  // only tiles that cross this row's causal limit need the mask
 #pragma unroll
@@ -393,29 +472,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 #pragma unroll
       for (int c = 4; c < kSC; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
       const float mxh = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
-#ifdef BPKV_TRACE
-      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[11], static_cast<unsigned long long>(clock64() - _tl));
-      _tl = clock64();
-#endif
+      BPKV_MARK(2);
       // exchange the half-row maxima (double-buffered; named barrier of the softmax warps)
       s_mx[((it & 1) * kSplit + half) * kBM + row] = mxh;
       {
-#ifdef BPKV_TRACE
-        BPKV_T0();
-#endif
-        asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kSoftmaxWarps) : "memory");
-#ifdef BPKV_TRACE
-        if (BPKV_TRACING && tid == 0) BPKV_TADD(5);
-#endif
+        // only the kSplit warps that share these rows (same warp % 4) meet here
+        asm volatile("bar.sync %0, %1;\n" ::"r"(2 + (warp & 3)), "n"(32 * kSplit) : "memory");
       }
       float mxr = s_mx[((it & 1) * kSplit) * kBM + row];
 #pragma unroll
       for (int h = 1; h < kSplit; ++h) mxr = fmaxf(mxr, s_mx[((it & 1) * kSplit + h) * kBM + row]);
       const float mx = mxr * p.scale_log2;
-#ifdef BPKV_TRACE
-      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[12], static_cast<unsigned long long>(clock64() - _tl));
-      _tl = clock64();
-#endif
+      BPKV_MARK(3);
       // lazy reference max: move it (rescale O, l) only when the row max grew by > threshold
       const bool need = mx > m_ref + kRescaleThreshold;
       float alpha = 1.f;
@@ -436,41 +504,54 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           tmem_st32(t_o + lane_base + oc0 + c0, o);
         }
       }
-#ifdef BPKV_TRACE
-      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[13], static_cast<unsigned long long>(clock64() - _tl));
-      _tl = clock64();
-#endif
+      BPKV_MARK(4);
       if (it >= 1) {  // the P buffer was last read by PV(it-1)
         wait(o_done(it - 1), ((it - 1) >> 1) & 1);
       }
+      BPKV_MARK(5);
       const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
+      const uint64_t sc2 = pk2(p.scale_log2, p.scale_log2), nm2 = pk2(-m_use, -m_use);
+      uint64_t sum2[2] = {0ull, 0ull};  // two independent packed sum chains (0ull = +0.0f pair)
       uint32_t hi[kSC / 2], lo[kSC / 2];
 #pragma unroll
       for (int c = 0; c < kSC; c += 2) {
-        const float a = fast_exp2(fmaf(s[c], p.scale_log2, -m_use));
-        const float bb = fast_exp2(fmaf(s[c + 1], p.scale_log2, -m_use));
-        sum4[(c >> 1) & 3] += a + bb;
-        split2<T>(a, bb, hi[c >> 1], lo[c >> 1]);
+        const uint64_t x2 = fma2(pk2(s[c], s[c + 1]), sc2, nm2);
+        uint64_t e2;
+        if ((c >> 1) % kEmuStride == kEmuStride - 1) {
+          e2 = exp2_poly2(x2);
+        } else {
+          float xa, xb;
+          up2(x2, xa, xb);
+          e2 = pk2(fast_exp2(xa), fast_exp2(xb));
+        }
+        sum2[(c >> 1) & 1] = add2(sum2[(c >> 1) & 1], e2);
+        float ea, eb;
+        up2(e2, ea, eb);
+        if constexpr (kBf16) {
+          // hi = bf16(e), lo = bf16(e - hi); bf16 -> fp32 is a 16-bit shift
+          const uint32_t h = pack2<T>(ea, eb);
+          const uint64_t l2 = sub2(e2, pk2(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u)));
+          float la, lb;
+          up2(l2, la, lb);
+          hi[c >> 1] = h;
+          lo[c >> 1] = pack2<T>(la, lb);
+        } else {
+          hi[c >> 1] = pack2<T>(ea, eb);
+          lo[c >> 1] = 0u;
+        }
       }
-#ifdef BPKV_TRACE
-      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[14], static_cast<unsigned long long>(clock64() - _tl));
-      _tl = clock64();
-#endif
+      BPKV_MARK(6);
       // P(it) -> TMEM: 32-bit column = token pair; hi part, then lo part kBN/2 columns on
       tc::tc_fence_after();
       const uint32_t pcol = tmem + kTmemP + lane_base + sc0 / 2;
       tc::tmem_st16(pcol, hi);
       if (kBf16) tc::tmem_st16(pcol + kBN / 2, lo);
-#ifdef BPKV_TRACE
-      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[15], static_cast<unsigned long long>(clock64() - _tl));
-      _tl = clock64();
-#endif
-      l_run += (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
-#ifdef BPKV_TRACE
-      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[9], static_cast<unsigned long long>(clock64() - _tl));
-      _tl = clock64();
-#endif
+      BPKV_MARK(7);
+      {
+        float sa, sb;
+        up2(add2(sum2[0], sum2[1]), sa, sb);
+        l_run += sa + sb;
+      }
       if (it == n_tiles - 1 && kv_end < (it + 1) * kBN) {
         // rows of the last page past kv_end hold whatever the pool page holds (P is
         // 0 there, but 0 * NaN is not): zero them in the V tile once it has landed
@@ -483,18 +564,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
               make_uint4(0, 0, 0, 0);
         }
       }
+      BPKV_MARK(8);
       tc::fence_proxy_async_smem();  // zeroed V rows -> visible to the tensor core
       tc::tc_fence_before();       // P stores in TMEM -> ordered before the MMA warp's issue
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(p_full(it)) : "memory");
-#ifdef BPKV_TRACE
-      if (BPKV_TRACING && tid == 0) atomicAdd(&g_prefill_trace[10], static_cast<unsigned long long>(clock64() - _tl));
-#endif
+      BPKV_MARK(9);
     }
     if (n_tiles > 0) wait(o_done(n_tiles - 1), ((n_tiles - 1) >> 1) & 1);
 #ifdef BPKV_TRACE
     if (BPKV_TRACING && tid == 0) {
-      atomicAdd(&g_prefill_trace[6], static_cast<unsigned long long>(clock64() - _tstart));
-      atomicAdd(&g_prefill_trace[7], static_cast<unsigned long long>(n_tiles));
+      atomicAdd(&g_prefill_trace[11], static_cast<unsigned long long>(clock64() - _tstart));
+      atomicAdd(&g_prefill_trace[10], static_cast<unsigned long long>(n_tiles));
     }
 #endif
     if (failed) *s_fail = 1;

@@ -3,23 +3,26 @@
 //
 // Same semantics as prefill.cu (causal, bottom-right aligned; K/V read from
 // 16-token pages through the block table, or dense varlen).  Per CTA:
-//   * 128 accumulator rows = 128/n_rep query tokens x the n_rep query heads of
-//     one KV head (a GQA group shares every K/V tile); 4 warps, thread i owns
-//     row i (= TMEM lane i), so the softmax needs no shuffles.
-//   * K/V tiles of 64 tokens (4 pages) land in a 4-deep shared-memory ring in
-//     the 128-byte-swizzled layout of the UMMA descriptors
-//     ([64-column block][token][128 B], 16-B chunk ^= token & 7).  Paged K/V
-//     come by TMA (cp.async.bulk.tensor, 4-D tensor map over the pool layer,
-//     one 16x64 box per page and half of head_dim), issued by one thread and
-//     tracked by transaction bytes on a per-buffer mbarrier; dense varlen K/V
-//     come by 16-byte cp.async that arrive on the same mbarriers.
-//   * S(j) = Q K(j)^T: M128 N64 K16 tcgen05.mma x 8 into one of two TMEM S
-//     buffers; S(j+1) is issued before the softmax of tile j runs.
-//   * softmax with a lazily updated reference max (log2 domain): P stays
-//     <= 2^8, so O only has to be rescaled in TMEM when a row max grows by more
-//     than 8; P goes to shared memory as bf16 hi + lo parts (fp16: one part).
-//   * O += P(j) V(j): M128 N128 K16 with V as an MN-major operand (the same
-//     tiles), accumulated in TMEM across all tiles; read once at the end.
+//   * two Q tiles (groups A and B) of 128 accumulator rows each; a row is one
+//     (query token, query head) pair of the n_rep heads of one KV head, so a
+//     GQA group shares every K/V tile, and both tiles share the K/V loads.
+//   * K/V tiles of 128 tokens (8 pages) land in 2-deep shared-memory rings in
+//     the 128-byte-swizzled layout of the UMMA descriptors ([64-column block]
+//     [token][128 B], 16-B chunk ^= token & 7).  Paged K/V come by TMA
+//     (cp.async.bulk.tensor, 4-D tensor map over the pool layer, one 16x64 box
+//     per page and half of head_dim, issued by 16 lanes of the load warp) and
+//     are tracked by transaction bytes on per-buffer mbarriers; dense varlen
+//     K/V come by 16-byte cp.async that arrive on the same mbarriers.
+//   * one warp issues every tcgen05.mma: S_g = Q_g K^T (M128 N128, Q and K in
+//     shared memory) and O_g += P_g V (M128 N128, P_g from TMEM, V as an
+//     MN-major operand) in the order PV_A(j) S_A(j+1) PV_B(j) S_B(j+1), so the
+//     softmax of one group runs while the tensor pipe works for the other.
+//   * softmax: 8 warps per group, 2 threads per row (64 columns each), online
+//     softmax in exp2 with a lazily moved reference max (O is rescaled in TMEM
+//     only when a row max grows by more than 2^8); 1 in 8 exponentials is
+//     evaluated on the FMA pipe by a polynomial to relieve the MUFU unit.  P
+//     is written over S in TMEM as bf16 hi + lo parts (fp16: one part), which
+//     keeps ~16 mantissa bits of each probability for the P.V product.
 // All waits are bounded; on a timeout the CTA stops, writes NaN rows and
 // still frees its TMEM.  No TMA multicast is used (the loads read this GPU's
 // own pool only).
@@ -45,7 +48,7 @@ struct PrefillTcParams {
 
 #ifdef BPKV_TRACE
 // Debug builds only (-DBPKV_TRACE): per-phase clock64 totals of CTA (0,0).
-__device__ unsigned long long g_prefill_trace[16];
+__device__ unsigned long long g_prefill_trace[32];
 #define BPKV_TRACING (blockIdx.x == 0)
 // consecutive checkpoints of thread 0: slot k accumulates the cycles since the previous mark
 #define BPKV_MARK(slot)                                                                          \
@@ -73,21 +76,27 @@ namespace {
 
 // An M=128 tcgen05.mma costs the same tensor-pipe time for any N <= 128 (measured:
 // ~64 cycles per K=16 step), so K/V tiles are 128 tokens: S = Q K^T runs at N=128.
+// Two 128-row Q tiles per CTA (groups A and B) share every K/V tile; each has its
+// own softmax warps, so the softmax of one group overlaps the other group's MMAs.
 constexpr int kD = 128, kBM = 128, kBN = 128, kDB = kD / 64;
-constexpr int kQBytes = kDB * kBM * 128;       // 32 KB
+constexpr int kGroups = 2, kRows = kGroups * kBM;  // accumulator rows per CTA
+constexpr int kQBytes = kDB * kBM * 128;       // 32 KB per Q tile
 constexpr int kKVBytes = kDB * kBN * 128;      // 32 KB per K or V tile
-constexpr int kNK = 3;                         // K ring depth (K(j) is free once S(j) completed)
-constexpr int kNV = 2;                         // V ring depth (V(j) is free once PV(j) completed)
-constexpr int kSplit = 4;                      // softmax threads per accumulator row
-constexpr int kSoftmaxWarps = 4 * kSplit;      // warps 0..15: softmax
-constexpr int kLoadWarp = kSoftmaxWarps;       // warp 8: TMA / cp.async loads
-constexpr int kMmaWarp = kSoftmaxWarps + 1;    // warp 9: tcgen05.mma issue
+constexpr int kNK = 2;                         // K ring depth (K(j) is free once S_B(j) completed)
+constexpr int kNV = 2;                         // V ring depth (V(j) is free once PV_B(j) completed)
+constexpr int kSplit = 2;                      // softmax threads per accumulator row
+constexpr int kGroupWarps = 4 * kSplit;        // softmax warps per group
+constexpr int kSoftmaxWarps = kGroups * kGroupWarps;  // warps 0..15
+constexpr int kLoadWarp = kSoftmaxWarps;       // warp 16: TMA / cp.async loads
+constexpr int kMmaWarp = kSoftmaxWarps + 1;    // warp 17: tcgen05.mma issue
 constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
 constexpr int kMaxPagesSmem = 2048;            // block-table entries staged in shared memory
-constexpr int kSmemBytes = kQBytes + (kNK + kNV) * kKVBytes + 1024 /*align*/ + 256 + 4 * kMaxPagesSmem +
-                            4 * 2 * kSplit * kBM /*row-max exchange*/ + 4 * kSplit * kBM /*row sums*/;
-constexpr uint32_t kTmemCols = 512;            // S0 [0,128) S1 [128,256) O [256,384) P hi [384,448) lo [448,512)
-constexpr uint32_t kTmemO = 256, kTmemP = 384;  // P: bf16 pairs per 32-bit column
+constexpr int kSmemBytes = kGroups * kQBytes + (kNK + kNV) * kKVBytes + 1024 /*align*/ + 256 + 4 * kMaxPagesSmem +
+                            4 * kGroups * 2 * kSplit * kBM /*row-max exchange*/ + 4 * kGroups * kSplit * kBM /*row sums*/;
+// TMEM: group g owns S_g [256g, 256g+128) and O_g [256g+128, 256g+256).  P_g (16-bit pairs)
+// overwrites S_g in place, chunk by chunk: the probabilities of S columns [32c, 32c+32) (tokens
+// 32c..32c+31) go to columns [32c, 32c+16) (hi parts) and [32c+16, 32c+32) (lo parts).
+constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 256 between rescales
 
 struct __align__(64) TcKernelArgs {
@@ -192,7 +201,7 @@ constexpr int kMaxRanked = 512;  // q-tile items ranked per CTA (n^2 / kThreads 
 __device__ __forceinline__ int item_tiles(const PrefillTcParams& p, int i) {
   const int b = i / p.tiles_per_req, qt = i % p.tiles_per_req;
   const int q0 = __ldg(p.cu_q + b), nq = __ldg(p.cu_q + b + 1) - q0;
-  const int tq = kBM / p.n_rep, tok0 = qt * tq;
+  const int tq = kRows / p.n_rep, tok0 = qt * tq;
   if (tok0 >= nq) return -1;
   const int sk = p.seqlens_k != nullptr ? __ldg(p.seqlens_k + b) : nq;
   const int last_tok = min(tok0 + tq, nq) - 1;
@@ -205,16 +214,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   const PrefillTcParams& p = args.p;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* qs = smem;                    // Q tile (A operand of S = Q K^T)
-  uint8_t* ks = qs + kQBytes;            // kNK buffers
-  uint8_t* vs = ks + kNK * kKVBytes;     // kNV buffers
+  uint8_t* qs = smem;                        // kGroups Q tiles
+  uint8_t* ks = qs + kGroups * kQBytes;      // kNK buffers
+  uint8_t* vs = ks + kNK * kKVBytes;         // kNV buffers
   uint64_t* bars = reinterpret_cast<uint64_t*>(vs + kNV * kKVBytes);
-  // bars: k_full[kNK], v_full[kNV], s_full[2], p_full[2], o_done[2], k_free[kNK], v_free[kNV]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * (kNK + kNV) + 6);
+  // bars: k_full[kNK], v_full[kNV], k_free[kNK], v_free[kNV], s_full[g], p_full[g], o_done[g]
+  constexpr int kBarCount = 2 * (kNK + kNV) + 3 * kGroups;
+  static_assert(kBarCount <= 30, "barrier area");
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBarCount);
   int* s_fail = reinterpret_cast<int*>(tmem_slot + 1);
   int* s_pages = reinterpret_cast<int*>(bars + 32);
-  float* s_mx = reinterpret_cast<float*>(s_pages + kMaxPagesSmem);  // [2 buffers][kSplit parts][kBM]
-  float* s_l = s_mx + 2 * kSplit * kBM;                                // [kSplit parts][kBM]
+  float* s_mx = reinterpret_cast<float*>(s_pages + kMaxPagesSmem);  // [group][2 buffers][kSplit][kBM]
+  float* s_l = s_mx + kGroups * 2 * kSplit * kBM;                      // [group][kSplit][kBM]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // ---- work item of this CTA: longest first ----
@@ -246,8 +257,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   const int qt = item % p.tiles_per_req;
   const int q0 = p.cu_q[b];
   const int nq = p.cu_q[b + 1] - q0;
-  const int TQ = kBM / p.n_rep;
-  const int tok0 = qt * TQ;
+  const int TQg = kBM / p.n_rep;  // query tokens per group
+  const int tok0 = qt * kGroups * TQg;
   if (tok0 >= nq) return;  // uniform across the CTA: before any barrier or TMEM use
   const int sk = PAGED ? p.seqlens_k[b] : nq;
   const T* qg = reinterpret_cast<const T*>(p.q);
@@ -255,62 +266,65 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   const T* vg = reinterpret_cast<const T*>(p.v);
   auto k_full = [&](int t) { return smem_u32(&bars[t % kNK]); };
   auto v_full = [&](int t) { return smem_u32(&bars[kNK + t % kNV]); };
-  auto s_full = [&](int j) { return smem_u32(&bars[kNK + kNV + (j & 1)]); };
-  auto p_full = [&](int j) { return smem_u32(&bars[kNK + kNV + 2 + (j & 1)]); };
-  auto o_done = [&](int j) { return smem_u32(&bars[kNK + kNV + 4 + (j & 1)]); };
-  auto k_free = [&](int t) { return smem_u32(&bars[kNK + kNV + 6 + t % kNK]); };
-  auto v_free = [&](int t) { return smem_u32(&bars[2 * kNK + kNV + 6 + t % kNV]); };
+  auto k_free = [&](int t) { return smem_u32(&bars[kNK + kNV + t % kNK]); };
+  auto v_free = [&](int t) { return smem_u32(&bars[2 * kNK + kNV + t % kNV]); };
+  auto s_full = [&](int g) { return smem_u32(&bars[2 * (kNK + kNV) + g]); };
+  auto p_full = [&](int g) { return smem_u32(&bars[2 * (kNK + kNV) + kGroups + g]); };
+  auto o_done = [&](int g) { return smem_u32(&bars[2 * (kNK + kNV) + 2 * kGroups + g]); };
 
   if (warp == 0) {
     tc::tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
-    for (int i = 0; i < kNK + kNV; ++i) tc::mbar_init(smem_u32(&bars[i]), PAGED ? 1u : 32u);
-    for (int i = 0; i < 2; ++i) {
-      tc::mbar_init(s_full(i), 1u);
-      tc::mbar_init(p_full(i), 32u * kSoftmaxWarps);
-      tc::mbar_init(o_done(i), 1u);
+    for (int i = 0; i < kNK; ++i) {
+      tc::mbar_init(k_full(i), PAGED ? 1u : 32u);
+      tc::mbar_init(k_free(i), 1u);
     }
-    for (int i = 0; i < kNK; ++i) tc::mbar_init(k_free(i), 1u);
-    for (int i = 0; i < kNV; ++i) tc::mbar_init(v_free(i), 1u);
+    for (int i = 0; i < kNV; ++i) {
+      tc::mbar_init(v_full(i), PAGED ? 1u : 32u);
+      tc::mbar_init(v_free(i), 1u);
+    }
+    for (int g = 0; g < kGroups; ++g) {
+      tc::mbar_init(s_full(g), 1u);
+      tc::mbar_init(p_full(g), 32u * kGroupWarps);
+      tc::mbar_init(o_done(g), 1u);
+    }
     *s_fail = 0;
     tc::fence_mbar_init();
   }
 
-  const int last_tok = min(tok0 + TQ, nq) - 1;
+  const int last_tok = min(tok0 + kGroups * TQg, nq) - 1;
   const int kv_end = p.causal ? min(sk, sk - nq + last_tok + 1) : sk;
   const int n_tiles = kv_end > 0 ? (kv_end + kBN - 1) / kBN : 0;
   if constexpr (PAGED) {
     const int np = min((kv_end + kPage - 1) / kPage, kMaxPagesSmem);
     for (int i = tid; i < np; i += kThreads) s_pages[i] = __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + i);
   }
-  tc::tc_fence_before();
-  __syncthreads();  // barriers initialised, TMEM address published, block table staged
-  tc::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  // ---- Q tile -> shared memory, 128-B swizzled K-major: row m = (token tok0 + m / n_rep,
-  //      head m % n_rep); [d-block][row][128 B] ----
-  if (warp < 4) {
-    const int m = tid;
-    const int tq = tok0 + m / p.n_rep, r = m % p.n_rep;
+  // ---- Q tiles -> shared memory, 128-B swizzled K-major: group g row m = (token
+  //      tok0 + g*TQg + m / n_rep, head m % n_rep); [d-block][row][128 B] per group ----
+  if (tid < kRows) {
+    const int g = tid / kBM, m = tid % kBM;
+    const int tq = tok0 + g * TQg + m / p.n_rep, r = m % p.n_rep;
     const uint4* src = reinterpret_cast<const uint4*>(qg + (static_cast<int64_t>(q0 + tq) * p.Hq + hkv * p.n_rep + r) * kD);
+    uint8_t* qd = qs + g * kQBytes;
 #pragma unroll
     for (int ch = 0; ch < kD / 8; ++ch) {
       const uint4 v = tq < nq ? __ldg(src + ch) : make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(qs + (ch >> 3) * (kBM * 128) + sw_off(m, ch & 7)) = v;
+      *reinterpret_cast<uint4*>(qd + (ch >> 3) * (kBM * 128) + sw_off(m, ch & 7)) = v;
     }
     tc::fence_proxy_async_smem();
   }
   tc::tc_fence_before();
-  __syncthreads();  // Q resident in shared memory
+  __syncthreads();  // barriers initialised, TMEM address published, block table and Q staged
   tc::tc_fence_after();
-  const uint32_t t_o = tmem + kTmemO;
-  auto t_s = [&](int j) { return tmem + static_cast<uint32_t>((j & 1) * kBN); };
+  const uint32_t tmem = *tmem_slot;
+  auto t_s = [&](int g) { return tmem + static_cast<uint32_t>(g * 256); };
+  auto t_o = [&](int g) { return tmem + static_cast<uint32_t>(g * 256 + 128); };
   constexpr bool kBf16 = SplitP<T>::value;
 
   if (warp >= kLoadWarp) {
-    // =================== producer warps: loads (warp 8), MMA issue (warp 9) ===================
+    // =================== producer warps: loads (warp 16), MMA issue (warp 17) ===================
     // K (which = 0) or V (which = 1) of tile t into its ring buffer
     auto load_kv = [&](int t, int which) {
       uint8_t* base = which == 0 ? ks + (t % kNK) * kKVBytes : vs + (t % kNV) * kKVBytes;
@@ -348,41 +362,43 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const uint64_t dq0 = tc::smem_desc_sw128(smem_u32(qs), 16, 1024);
     const uint64_t dk0 = tc::smem_desc_sw128(smem_u32(ks), 16, 1024);
     const uint64_t dv0 = tc::smem_desc_sw128(smem_u32(vs), kBN * 128, 1024);
-    auto issue_s = [&](int j) {  // S(j) = Q K(j)^T, both operands from shared memory
+    auto issue_s = [&](int g, int j) {  // S_g(j) = Q_g K(j)^T, both operands in shared memory
       tc::tc_fence_after();
+      const uint64_t qb = dq0 + static_cast<uint64_t>((g * kQBytes) >> 4);
       const uint64_t kb = dk0 + static_cast<uint64_t>(((j % kNK) * kKVBytes) >> 4);
 #pragma unroll
       for (int kk = 0; kk < kD / 16; ++kk) {
         const uint64_t qoff = static_cast<uint64_t>(((kk >> 2) * (kBM * 128) + (kk & 3) * 32) >> 4);
         const uint64_t kboff = static_cast<uint64_t>(((kk >> 2) * (kBN * 128) + (kk & 3) * 32) >> 4);
-        tc::mma_f16(t_s(j), dq0 + qoff, kb + kboff, id_s, kk > 0 ? 1u : 0u);
+        tc::mma_f16(t_s(g), qb + qoff, kb + kboff, id_s, kk > 0 ? 1u : 0u);
       }
-      tc::mma_commit(s_full(j));
+      tc::mma_commit(s_full(g));
     };
-    auto issue_o = [&](int j) {  // O += P(j) V(j), P from TMEM (bf16: hi part then lo part)
+    auto issue_o = [&](int g, int j) {  // O_g += P_g(j) V(j), P_g from TMEM (bf16: hi part then lo part)
       tc::tc_fence_after();
       const uint64_t vb = dv0 + static_cast<uint64_t>(((j % kNV) * kKVBytes) >> 4);
       const int parts = kBf16 ? 2 : 1;
       for (int part = 0; part < parts; ++part) {
-        const uint32_t pa = tmem + kTmemP + part * (kBN / 2);
 #pragma unroll
-        for (int kk = 0; kk < kBN / 16; ++kk)
-          tc::mma_f16_ts(t_o, pa + kk * 8, vb + static_cast<uint64_t>((kk * 16 * 128) >> 4), id_o,
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint32_t pa = t_s(g) + (kk >> 1) * 32 + part * 16 + (kk & 1) * 8;
+          tc::mma_f16_ts(t_o(g), pa, vb + static_cast<uint64_t>((kk * 16 * 128) >> 4), id_o,
                          (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+        }
       }
-      tc::mma_commit(o_done(j));
+      tc::mma_commit(o_done(g));
     };
     bool ok = true;
     if (warp == kLoadWarp) {
       for (int t = 0; t < kNK - 1 && t < n_tiles; ++t) load_kv(t, 0);
       for (int t = 0; t < kNV - 1 && t < n_tiles; ++t) load_kv(t, 1);
       for (int j = 0; ok && j < n_tiles; ++j) {
-        if (j + kNK - 1 < n_tiles) {  // K buffer of tile j-1: free once S(j-1) completed
+        if (j + kNK - 1 < n_tiles) {  // K buffer of tile j-1: free once S_B(j-1) completed
           if (j >= 1) ok = tc::mbar_wait(k_free(j - 1), ((j - 1) / kNK) & 1);
           if (!ok) break;
           load_kv(j + kNK - 1, 0);
         }
-        if (j + kNV - 1 < n_tiles) {  // V buffer of tile j-1: free once PV(j-1) completed
+        if (j + kNV - 1 < n_tiles) {  // V buffer of tile j-1: free once PV_B(j-1) completed
           if (j >= 1) ok = tc::mbar_wait(v_free(j - 1), ((j - 1) / kNV) & 1);
           if (!ok) break;
           load_kv(j + kNV - 1, 1);
@@ -390,14 +406,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         __syncwarp();
       }
     } else {
-      // Tensor-pipe order: S(0) S(1) | PV(0) S(2) | PV(1) S(3) | ...  S(j+2) reuses the S buffer
-      // of S(j), which softmax(j) has read before it published P(j); issuing it right behind
-      // PV(j) (instead of ahead of PV(j-1)) has S ready when the softmax warps finish P(j).
-      for (int j = 0; ok && j < 2 && j < n_tiles; ++j) {
-        ok = tc::mbar_wait(k_full(j), (j / kNK) & 1);
+      // Tensor-pipe order: S_A(0) S_B(0) | PV_A(0) S_A(1) PV_B(0) S_B(1) | PV_A(1) S_A(2) ...
+      // S_g(j+1) overwrites P_g(j), so it is issued once PV_g(j) has completed; between
+      // P_g(j) and PV_g(j+1) the pipe runs the other group's PV and S (the window in
+      // which group g computes its softmax).
+      if (n_tiles > 0) {
+        ok = tc::mbar_wait(k_full(0), 0);
         if (ok && lane == 0) {
-          issue_s(j);
-          tc::mma_commit(k_free(j));
+          issue_s(0, 0);
+          issue_s(1, 0);
+          tc::mma_commit(k_free(0));
         }
         __syncwarp();
       }
@@ -405,42 +423,61 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       long long _tm = clock64();
 #endif
       for (int j = 0; ok && j < n_tiles; ++j) {
-        BPKV_MARK_MMA(15);
-        ok = tc::mbar_wait(p_full(j), (j >> 1) & 1);  // softmax(j) wrote P(j), done with S(j)
+        const uint32_t par = j & 1;
+        BPKV_MARK_MMA(20);
+        ok = tc::mbar_wait(p_full(0), par) && tc::mbar_wait(v_full(j), (j / kNV) & 1);
         if (!ok) break;
-        BPKV_MARK_MMA(12);
-        ok = tc::mbar_wait(v_full(j), (j / kNV) & 1);
+        BPKV_MARK_MMA(21);
+        if (lane == 0) issue_o(0, j);
+        __syncwarp();
+        BPKV_MARK_MMA(22);
+        if (j + 1 < n_tiles) {
+          ok = tc::mbar_wait(k_full(j + 1), ((j + 1) / kNK) & 1) && tc::mbar_wait(o_done(0), par);
+          if (!ok) break;
+          BPKV_MARK_MMA(23);
+          if (lane == 0) issue_s(0, j + 1);
+          __syncwarp();
+          BPKV_MARK_MMA(24);
+        }
+        ok = tc::mbar_wait(p_full(1), par);
         if (!ok) break;
-        BPKV_MARK_MMA(13);
+        BPKV_MARK_MMA(25);
         if (lane == 0) {
-          issue_o(j);
+          issue_o(1, j);
           tc::mma_commit(v_free(j));
         }
-        BPKV_MARK_MMA(9);
-        if (j + 2 < n_tiles) {
-          ok = tc::mbar_wait(k_full(j + 2), ((j + 2) / kNK) & 1);
-          if (!ok) break;
-          BPKV_MARK_MMA(14);
-          if (lane == 0) {
-            issue_s(j + 2);
-            tc::mma_commit(k_free(j + 2));
-          }
-        }
         __syncwarp();
+        BPKV_MARK_MMA(26);
+        if (j + 1 < n_tiles) {
+          ok = tc::mbar_wait(o_done(1), par);
+          if (!ok) break;
+          BPKV_MARK_MMA(27);
+          if (lane == 0) {
+            issue_s(1, j + 1);
+            tc::mma_commit(k_free(j + 1));
+          }
+          __syncwarp();
+        }
       }
     }
     if (!ok) *s_fail = 1;
   } else {
-    // ============ softmax warps: kSplit threads per accumulator row ============
-    // warp w handles rows (w % 4)*32 + lane (TMEM lanes of its sub-partition) and
-    // column part h = w / 4: S columns [h*kBN/kSplit, ...), O columns [h*kD/kSplit, ...).
-    const int half = warp / 4;
-    const int row = (warp % 4) * 32 + lane;
-    const int tok = tok0 + row / p.n_rep;
+    // ============ softmax warps: group g = warp / 8, kSplit threads per accumulator row ============
+    // warp w of group g handles rows (w % 4)*32 + lane (TMEM lanes of its sub-partition) and
+    // column half h = (w % 8) / 4: S columns [64h, 64h+64) of S_g, O columns [64h, 64h+64) of O_g.
+    const int g = warp / kGroupWarps;
+    const int half = (warp % kGroupWarps) / 4;
+    const int rq = warp % 4;
+    const int row = rq * 32 + lane;
+    const int tok = tok0 + g * TQg + row / p.n_rep;
     const int lim = p.causal ? (tok < nq ? sk - nq + tok : sk - 1) : sk - 1;
-    const uint32_t lane_base = static_cast<uint32_t>((warp % 4) * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>(rq * 32) << 16;
     constexpr int kSC = kBN / kSplit, kOC = kD / kSplit;
+    static_assert(kSC == 64 && kOC == 64, "two x32 TMEM loads per thread and tile");
     const int sc0 = half * kSC, oc0 = half * kOC;
+    const uint32_t ts = t_s(g) + lane_base + sc0, to = t_o(g) + lane_base + oc0;
+    const uint32_t bar_id = 2 + g * 4 + rq;  // the kSplit warps sharing these rows
+    float* mxg = s_mx + g * 2 * kSplit * kBM;
     float m_ref = -INFINITY, l_run = 0.f;
     // A failed (timed-out) wait only sets `failed`: the loop keeps its shape, so
     // every softmax warp still reaches every named barrier, and later waits are
@@ -456,32 +493,34 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const long long _tstart = _tl;
 #endif
     for (int it = 0; it < n_tiles; ++it) {
-      wait(s_full(it), (it >> 1) & 1);
+      // S_g(it) complete; its commit also covers PV_g(it-1), so O_g and the P_g area are free
+      wait(s_full(g), it & 1);
       BPKV_MARK(0);
       tc::tc_fence_after();
-      float s[kSC];
-      static_assert(kSC == 32, "one x32 TMEM load per thread and tile");
-      tc::tmem_ld32(t_s(it) + lane_base + sc0, s);
-      BPKV_MARK(1);
       const int tbase = it * kBN + sc0;
-      if (tbase + kSC - 1 > lim) {  // only tiles that cross this row's causal limit need the mask
+      const bool crosses = tbase + kSC - 1 > lim;  // only tiles that cross this row's causal limit need the mask
+      // pass 1: row maximum over this thread's 64 columns (32 at a time; S is read again in pass 2)
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent max chains
 #pragma unroll
-        for (int c = 0; c < kSC; ++c) s[c] = (tbase + c <= lim) ? s[c] : -INFINITY;
+      for (int c0 = 0; c0 < kSC; c0 += 32) {
+        float s[32];
+        tc::tmem_ld32(ts + c0, s);
+        if (crosses) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) s[c] = (tbase + c0 + c <= lim) ? s[c] : -INFINITY;
+        }
+#pragma unroll
+        for (int c = 0; c < 32; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
       }
-      float mx4[4] = {s[0], s[1], s[2], s[3]};  // four independent max chains
-#pragma unroll
-      for (int c = 4; c < kSC; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+      BPKV_MARK(1);
       const float mxh = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       BPKV_MARK(2);
-      // exchange the half-row maxima (double-buffered; named barrier of the softmax warps)
-      s_mx[((it & 1) * kSplit + half) * kBM + row] = mxh;
-      {
-        // only the kSplit warps that share these rows (same warp % 4) meet here
-        asm volatile("bar.sync %0, %1;\n" ::"r"(2 + (warp & 3)), "n"(32 * kSplit) : "memory");
-      }
-      float mxr = s_mx[((it & 1) * kSplit) * kBM + row];
+      // exchange the half-row maxima with the partner warp (double-buffered)
+      mxg[((it & 1) * kSplit + half) * kBM + row] = mxh;
+      asm volatile("bar.sync %0, %1;\n" ::"r"(bar_id), "n"(32 * kSplit) : "memory");
+      float mxr = mxg[((it & 1) * kSplit) * kBM + row];
 #pragma unroll
-      for (int h = 1; h < kSplit; ++h) mxr = fmaxf(mxr, s_mx[((it & 1) * kSplit + h) * kBM + row]);
+      for (int h = 1; h < kSplit; ++h) mxr = fmaxf(mxr, mxg[((it & 1) * kSplit + h) * kBM + row]);
       const float mx = mxr * p.scale_log2;
       BPKV_MARK(3);
       // lazy reference max: move it (rescale O, l) only when the row max grew by > threshold
@@ -493,84 +532,87 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         l_run *= alpha;
       }
       if (it > 0 && __any_sync(0xffffffffu, need)) {
-        wait(o_done(it - 1), ((it - 1) >> 1) & 1);  // O last written by PV(it-1)
-        tc::tc_fence_after();
 #pragma unroll
         for (int c0 = 0; c0 < kOC; c0 += 32) {
           float o[32];
-          tc::tmem_ld32(t_o + lane_base + oc0 + c0, o);
+          tc::tmem_ld32(to + c0, o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(t_o + lane_base + oc0 + c0, o);
+          tmem_st32(to + c0, o);
         }
       }
       BPKV_MARK(4);
-      if (it >= 1) {  // the P buffer was last read by PV(it-1)
-        wait(o_done(it - 1), ((it - 1) >> 1) & 1);
-      }
-      BPKV_MARK(5);
       const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
       const uint64_t sc2 = pk2(p.scale_log2, p.scale_log2), nm2 = pk2(-m_use, -m_use);
       uint64_t sum2[2] = {0ull, 0ull};  // two independent packed sum chains (0ull = +0.0f pair)
-      uint32_t hi[kSC / 2], lo[kSC / 2];
 #pragma unroll
-      for (int c = 0; c < kSC; c += 2) {
-        const uint64_t x2 = fma2(pk2(s[c], s[c + 1]), sc2, nm2);
-        uint64_t e2;
-        if ((c >> 1) % kEmuStride == kEmuStride - 1) {
-          e2 = exp2_poly2(x2);
-        } else {
-          float xa, xb;
-          up2(x2, xa, xb);
-          e2 = pk2(fast_exp2(xa), fast_exp2(xb));
+      for (int c0 = 0; c0 < kSC; c0 += 32) {
+        // pass 2, chunk by chunk: S columns [c0, c0+32) -> P hi / lo in the same 32 columns
+        float s[32];
+        tc::tmem_ld32(ts + c0, s);
+        if (crosses) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) s[c] = (tbase + c0 + c <= lim) ? s[c] : -INFINITY;
         }
-        sum2[(c >> 1) & 1] = add2(sum2[(c >> 1) & 1], e2);
-        float ea, eb;
-        up2(e2, ea, eb);
-        if constexpr (kBf16) {
-          // hi = bf16(e), lo = bf16(e - hi); bf16 -> fp32 is a 16-bit shift
-          const uint32_t h = pack2<T>(ea, eb);
-          const uint64_t l2 = sub2(e2, pk2(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u)));
-          float la, lb;
-          up2(l2, la, lb);
-          hi[c >> 1] = h;
-          lo[c >> 1] = pack2<T>(la, lb);
-        } else {
-          hi[c >> 1] = pack2<T>(ea, eb);
-          lo[c >> 1] = 0u;
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int c = 0; c < 32; c += 2) {
+          const uint64_t x2 = fma2(pk2(s[c], s[c + 1]), sc2, nm2);
+          uint64_t e2;
+          if ((c >> 1) % kEmuStride == kEmuStride - 1) {
+            e2 = exp2_poly2(x2);
+          } else {
+            float xa, xb;
+            up2(x2, xa, xb);
+            e2 = pk2(fast_exp2(xa), fast_exp2(xb));
+          }
+          sum2[(c >> 1) & 1] = add2(sum2[(c >> 1) & 1], e2);
+          float ea, eb;
+          up2(e2, ea, eb);
+          if constexpr (kBf16) {
+            // hi = bf16(e), lo = bf16(e - hi); bf16 -> fp32 is a 16-bit shift
+            const uint32_t h = pack2<T>(ea, eb);
+            const uint64_t l2 = sub2(e2, pk2(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u)));
+            float la, lb;
+            up2(l2, la, lb);
+            hi[c >> 1] = h;
+            lo[c >> 1] = pack2<T>(la, lb);
+          } else {
+            hi[c >> 1] = pack2<T>(ea, eb);
+            lo[c >> 1] = 0u;
+          }
         }
+        // P_g(it) over this chunk of S_g: token pair per 32-bit column, hi parts then lo parts
+        tc::tmem_st16(ts + c0, hi);
+        if (kBf16) tc::tmem_st16(ts + c0 + 16, lo);
       }
-      BPKV_MARK(6);
-      // P(it) -> TMEM: 32-bit column = token pair; hi part, then lo part kBN/2 columns on
-      tc::tc_fence_after();
-      const uint32_t pcol = tmem + kTmemP + lane_base + sc0 / 2;
-      tc::tmem_st16(pcol, hi);
-      if (kBf16) tc::tmem_st16(pcol + kBN / 2, lo);
-      BPKV_MARK(7);
+      BPKV_MARK(5);
       {
         float sa, sb;
         up2(add2(sum2[0], sum2[1]), sa, sb);
         l_run += sa + sb;
       }
-      if (it == n_tiles - 1 && kv_end < (it + 1) * kBN) {
+      bool zeroed = false;
+      if (g == 0 && it == n_tiles - 1 && kv_end < (it + 1) * kBN) {
         // rows of the last page past kv_end hold whatever the pool page holds (P is
-        // 0 there, but 0 * NaN is not): zero them in the V tile once it has landed
+        // 0 there, but 0 * NaN is not): zero them in the V tile once it has landed;
+        // PV_A(it) and PV_B(it) both come after this group's arrival on p_full
         wait(v_full(it), (it / kNV) & 1);
         uint8_t* vb = vs + (it % kNV) * kKVBytes;
         const int first = kv_end - it * kBN;
-        for (int e = tid; e < (kBN - first) * kDB * 8; e += 32 * kSoftmaxWarps) {
+        for (int e = tid; e < (kBN - first) * kDB * 8; e += 32 * kGroupWarps) {
           const int tt = first + e / (kDB * 8), rem = e % (kDB * 8);
           *reinterpret_cast<uint4*>(vb + (rem >> 3) * (kBN * 128) + tt * 128 + (rem & 7) * 16) =
               make_uint4(0, 0, 0, 0);
         }
+        zeroed = true;
       }
-      BPKV_MARK(8);
-      tc::fence_proxy_async_smem();  // zeroed V rows -> visible to the tensor core
-      tc::tc_fence_before();       // P stores in TMEM -> ordered before the MMA warp's issue
-      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(p_full(it)) : "memory");
-      BPKV_MARK(9);
+      if (zeroed) tc::fence_proxy_async_smem();  // zeroed V rows -> visible to the tensor core
+      tc::tc_fence_before();                     // P stores in TMEM -> ordered before the MMA warp's issue
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(p_full(g)) : "memory");
+      BPKV_MARK(6);
     }
-    if (n_tiles > 0) wait(o_done(n_tiles - 1), ((n_tiles - 1) >> 1) & 1);
+    if (n_tiles > 0) wait(o_done(g), (n_tiles - 1) & 1);
 #ifdef BPKV_TRACE
     if (BPKV_TRACING && tid == 0) {
       atomicAdd(&g_prefill_trace[11], static_cast<unsigned long long>(clock64() - _tstart));
@@ -580,33 +622,36 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     if (failed) *s_fail = 1;
     const bool ok = !failed;
     // ---- epilogue: row sum of both halves, O / l from TMEM ----
-    s_l[half * kBM + row] = l_run;
-    asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kSoftmaxWarps) : "memory");
+    float* lg = s_l + g * kSplit * kBM;
+    lg[half * kBM + row] = l_run;
+    asm volatile("bar.sync %0, %1;\n" ::"r"(bar_id), "n"(32 * kSplit) : "memory");
     float l_row = 0.f;
 #pragma unroll
-    for (int h = 0; h < kSplit; ++h) l_row += s_l[h * kBM + row];
-    float acc[kOC];
+    for (int h = 0; h < kSplit; ++h) l_row += lg[h * kBM + row];
     const bool all_ok = __all_sync(0xffffffffu, ok);  // before any divergent branch
-    if (all_ok && n_tiles > 0) {
-      tc::tc_fence_after();
+    const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
+    const float nan = __int_as_float(0x7fc00000);
+    T* dst = reinterpret_cast<T*>(p.out) +
+             (static_cast<int64_t>(q0 + tok) * p.Hq + hkv * p.n_rep + row % p.n_rep) * kD + oc0;
+    if (all_ok && n_tiles > 0) tc::tc_fence_after();
 #pragma unroll
-      for (int c0 = 0; c0 < kOC; c0 += 32) tc::tmem_ld32(t_o + lane_base + oc0 + c0, acc + c0);
-    } else {
+    for (int c0 = 0; c0 < kOC; c0 += 32) {
+      float acc[32];
+      if (all_ok && n_tiles > 0) {
+        tc::tmem_ld32(to + c0, acc);
+      } else {
 #pragma unroll
-      for (int i = 0; i < kOC; ++i) acc[i] = 0.f;
-    }
-    if (tok < nq) {
-      const float inv = l_row > 0.f ? 1.f / l_row : 0.f;
-      const float nan = __int_as_float(0x7fc00000);
-      T* dst = reinterpret_cast<T*>(p.out) +
-               (static_cast<int64_t>(q0 + tok) * p.Hq + hkv * p.n_rep + row % p.n_rep) * kD + oc0;
+        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+      }
+      if (tok < nq) {
 #pragma unroll
-      for (int c = 0; c < kOC; c += 8) {
-        float v[8];
+        for (int c = 0; c < 32; c += 8) {
+          float v[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = all_ok ? acc[c + i] * inv : nan;
-        *reinterpret_cast<uint4*>(dst + c) =
-            make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]), pack2<T>(v[6], v[7]));
+          for (int i = 0; i < 8; ++i) v[i] = all_ok ? acc[c + i] * inv : nan;
+          *reinterpret_cast<uint4*>(dst + c0 + c) =
+              make_uint4(pack2<T>(v[0], v[1]), pack2<T>(v[2], v[3]), pack2<T>(v[4], v[5]), pack2<T>(v[6], v[7]));
+        }
       }
     }
   }
@@ -660,7 +705,7 @@ bool make_page_map(CUtensorMap* map, const void* base, int Hkv, int64_t page_str
 int prefill_tc_launch(PrefillTcParams& p, int head_dim, int dtype, int max_seqlen_q, bool paged, cudaStream_t st) {
   if (head_dim != kD || (dtype != BPKV_BF16 && dtype != BPKV_F16) || kBM % p.n_rep != 0) return BPKV_ERR_UNSUPPORTED;
   if (paged && (p.page_stride * 2) % 16 != 0) return BPKV_ERR_UNSUPPORTED;
-  const int TQ = kBM / p.n_rep;
+  const int TQ = kRows / p.n_rep;  // query tokens per CTA
   p.tiles_per_req = (max_seqlen_q + TQ - 1) / TQ;
   if (p.tiles_per_req == 0 || p.B == 0) return BPKV_OK;
   TcKernelArgs args;
@@ -703,10 +748,10 @@ int prefill_tc_launch(PrefillTcParams& p, int head_dim, int dtype, int max_seqle
 
 #ifdef BPKV_TRACE
 extern "C" BPKV_API int bpkv_debug_prefill_trace(unsigned long long* out, int n, int reset) {
-  if (n > 16) n = 16;
+  if (n > 32) n = 32;
   if (cudaMemcpyFromSymbol(out, bpkv::g_prefill_trace, sizeof(unsigned long long) * n) != cudaSuccess) return 3;
   if (reset) {
-    unsigned long long z[16] = {0};
+    unsigned long long z[32] = {0};
     cudaMemcpyToSymbol(bpkv::g_prefill_trace, z, sizeof(z));
   }
   return 0;

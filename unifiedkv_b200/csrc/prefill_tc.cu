@@ -501,16 +501,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const bool crosses = tbase + kSC - 1 > lim;  // only tiles that cross this row's causal limit need the mask
       // pass 1: row maximum over this thread's 64 columns (32 at a time; S is read again in pass 2)
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent max chains
-#pragma unroll
-      for (int c0 = 0; c0 < kSC; c0 += 32) {
-        float s[32];
-        tc::tmem_ld32(ts + c0, s);
+      {
+        float s[kSC];
+        tc::tmem_ld32x2(ts, ts + 32, s, s + 32);
         if (crosses) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) s[c] = (tbase + c0 + c <= lim) ? s[c] : -INFINITY;
+          for (int c = 0; c < kSC; ++c) s[c] = (tbase + c <= lim) ? s[c] : -INFINITY;
         }
 #pragma unroll
-        for (int c = 0; c < 32; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+        for (int c = 0; c < kSC; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
       }
       BPKV_MARK(1);
       const float mxh = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));

@@ -22,21 +22,9 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "score_tc.cuh"
 
 namespace bpkv {
-
-struct ScoreTcParams {
-  const void* k;
-  const void* q;
-  int Hkv, n_rep, W, Wp, Lm, Tm, sink, n_chunks;
-  int64_t k_sh, k_st, q_sh, q_st;
-  float scale_log2;
-  float2* ml_part;
-  const float2* ml;
-  float* headmax;
-};
-// tcgen05 scoring passes (compress_tc.cu); BPKV_ERR_UNSUPPORTED if the shape does not fit.
-int score_tc_pass(ScoreTcParams& p, int head_dim, int dtype, int pass, cudaStream_t st);
 
 namespace {
 
@@ -503,6 +491,7 @@ int launch_score(ScoreParams& p, float* out, int N, int smooth, cudaStream_t st)
     t.q_sh = p.q_sh;
     t.q_st = p.q_st;
     t.scale_log2 = p.scale_log2;
+    t.n_chunks = p.n_chunks;  // workspace capacity; pass 1 sets the ranges actually used
     t.ml_part = p.ml_part;
     t.ml = p.ml;
     t.headmax = p.headmax;

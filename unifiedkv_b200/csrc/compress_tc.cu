@@ -39,7 +39,8 @@ constexpr int kLoadWarp = kComputeWarps, kMmaWarp = kComputeWarps + 1;
 constexpr int kThreads = (kComputeWarps + 2) * 32;
 constexpr int kSmem = kQBytes + kNK * kKBytes + 1024 /*align*/ + 256 /*barriers*/ + kRowsMax * 4 /*row offsets*/ +
                       2 * 4 * kTok * 4 /*head-max exchange*/;
-constexpr int kEmu = 8;                        // every kEmu-th exponential pair on the FMA pipe
+// every kEmu1-th / kEmu2-th exponential pair of pass 1 / pass 2 goes to the FMA pipe
+constexpr int kEmu1 = 8, kEmu2 = 8;
 
 struct __align__(64) ScoreTcArgs {
   CUtensorMap tmap_k;  // (d, token, kv head) over K, box (64, 128, 1), 128-B swizzle
@@ -81,7 +82,7 @@ __device__ void load_q(const ScoreTcParams& p, uint8_t* qs, int g, int rows_pad,
 
 // exp2 of 32 values x = s * scale + offs[c] (pre-negated per-value offsets, 8-byte aligned) or
 // x = s * scale - off (one scalar), summed into a packed pair of partial sums
-template <bool kPerValueOff>
+template <bool kPerValueOff, int kEmu>
 __device__ __forceinline__ uint64_t exp2_sum32(const float* s, float scale, const float* offs, float off,
                                                uint64_t acc) {
   const uint64_t sc2 = pk2(scale, scale);
@@ -250,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_cons
               load(c0, a);
 #pragma unroll
               for (int c = 0; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], a[c]);
-              acc = exp2_sum32<false>(a, p.scale_log2, nullptr, ref, acc);
+              acc = exp2_sum32<false, kEmu1>(a, p.scale_log2, nullptr, ref, acc);
             }
             mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
             float sa, sb;
@@ -328,7 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_cons
 #pragma unroll
                 for (int c = 16; c < 32; ++c) a[c] = -INFINITY;
               }
-              acc = exp2_sum32<true>(a, p.scale_log2, s_off + c0, 0.f, acc);
+              acc = exp2_sum32<true, kEmu2>(a, p.scale_log2, s_off + c0, 0.f, acc);
             }
             float sa, sb;
             up2(acc, sa, sb);

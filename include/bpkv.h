@@ -189,6 +189,23 @@ BPKV_API int bpkv_block_score(const void* k, const void* q_obs, float* block_sco
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------ *
+ * Per-KV-head block scores (the "top 25% of blocks per KV head" reading of
+ * the compression benchmark).  The reference has no such mode: its score is
+ * shared across KV heads (max over all q heads, core/compress.py:116-130,
+ * core/scheduler.py:565-592).  Here KV head g keeps its own row
+ *   S_g[t] = max_{h in group g} mean_i A[h, i, t],  block_g[n] = sum_t S_g[t],
+ * smoothed per row as above.  block_scores: fp32 [num_kv_heads][N].  Other
+ * arguments and the workspace as bpkv_block_score.
+ * ------------------------------------------------------------------------ */
+BPKV_API int bpkv_block_score_per_kv_head(const void* k, const void* q_obs, float* block_scores,
+                     int num_kv_heads, int num_q_heads, int L, int window, int head_dim,
+                     int sink_len, int obs_len,
+                     int64_t k_stride_h, int64_t k_stride_t,
+                     int64_t q_stride_h, int64_t q_stride_t,
+                     float softmax_scale, int smooth, int dtype,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------ *
  * Deterministic top-k block selection.
  * Replaces torch.topk + sort (core/compress.py:140-142) and
  * torch.topk + sorted(set(...)) (core/scheduler.py:615-616); ties are broken by
@@ -197,6 +214,12 @@ BPKV_API int bpkv_block_score(const void* k, const void* q_obs, float* block_sco
  * n <= 49152.  NaN scores rank above every number (as torch.topk).
  * ------------------------------------------------------------------------ */
 BPKV_API int bpkv_topk_select(const float* scores, int n, int k, int32_t* selected, void* stream);
+
+/* Batched form: rows b = 0..batch-1 of scores [batch][n] -> selected
+ * [batch][k], one independent selection per row (per-KV-head mode: one row
+ * per KV head).  Same rules as bpkv_topk_select; no reference counterpart. */
+BPKV_API int bpkv_topk_select_batched(const float* scores, int n, int k, int batch, int32_t* selected,
+                     void* stream);
 
 /* ------------------------------------------------------------------------ *
  * Compacting writeback of one layer into freshly allocated pool pages.
@@ -224,6 +247,21 @@ BPKV_API int bpkv_page_compact(const void* k_src, const void* v_src, void* k_dst
                       int L, int sink_len, int obs_len, int num_kv_heads, int head_dim,
                       int64_t src_stride_h, int64_t src_stride_t, int64_t page_stride,
                       int64_t dst_stride_t, int64_t dst_stride_h, int dtype, void* stream);
+
+/* Per-KV-head compaction: KV head h takes its mid blocks from
+ * selected + h * selected_stride_h (int32 [num_kv_heads][>= k_blocks], ascending
+ * per head), so every head keeps its own blocks in the same destination pages;
+ * all heads share the effective length.  Decode over such pages is unchanged
+ * (keys already carry their positions through RoPE).  Other arguments as
+ * bpkv_page_compact.  No reference counterpart (its selection is shared
+ * across KV heads, core/scheduler.py:735-799). */
+BPKV_API int bpkv_page_compact_per_kv_head(const void* k_src, const void* v_src, void* k_dst, void* v_dst,
+                     const int32_t* selected, int64_t selected_stride_h, int k_blocks,
+                     const int32_t* dst_pages, int L, int sink_len, int obs_len,
+                     int num_kv_heads, int head_dim,
+                     int64_t src_stride_h, int64_t src_stride_t,
+                     int64_t page_stride, int64_t dst_stride_t, int64_t dst_stride_h,
+                     int dtype, void* stream);
 
 /* ------------------------------------------------------------------------ *
  * Paged chunked-prefill attention (causal, bottom-right aligned).

@@ -11,6 +11,9 @@ Restates:
     core/scheduler.py:615-616) with the tie order fixed to lowest index first;
   * writeback source order: core/scheduler.py:666-799 (sink, selected mid blocks
     padded to 16, observation tail; slots past effective_len untouched).
+Per-KV-head mode (no reference counterpart; the reference's selection is shared
+across KV heads): the same score with the max taken only over the q heads of
+one KV group, then the same top-k and writeback rules applied per KV head.
 """
 from __future__ import annotations
 
@@ -43,8 +46,8 @@ def compress_k_blocks(N, sink, obs, budget=0, ratio=0.2, B=16):
     return max(1, int(math.floor(ratio * N)))
 
 
-def block_scores(K, Q, sink, obs, scale=None, smooth="always", dtype=np.float64):
-    """K [h_kv, L, d], Q [h_q, W, d] -> block scores [N] (dtype)."""
+def block_scores(K, Q, sink, obs, scale=None, smooth="always", dtype=np.float64, per_kv_head=False):
+    """K [h_kv, L, d], Q [h_q, W, d] -> block scores [N] (dtype), or [h_kv, N] per KV head."""
     K = np.asarray(K, dtype)
     Q = np.asarray(Q, dtype)
     h_kv, L, d = K.shape
@@ -58,18 +61,20 @@ def block_scores(K, Q, sink, obs, scale=None, smooth="always", dtype=np.float64)
         return np.zeros(0, dtype)
     pad = np.zeros((h_kv, N * 16, d), dtype)
     pad[:, :Lm] = mid
-    S = np.full(N * 16, -np.inf, dtype)
+    S = np.full((h_kv, N * 16), -np.inf, dtype)  # per KV group: max over its q heads
     for hq in range(h_q):
         s = Q[hq] @ pad[hq // n_rep].T * dtype(scale)  # [W, T]
         s = s - s.max(axis=1, keepdims=True)
         p = np.exp(s)
         p /= p.sum(axis=1, keepdims=True)
-        S = np.maximum(S, p.mean(axis=0))
-    blk = S.reshape(N, 16).sum(axis=1)
+        S[hq // n_rep] = np.maximum(S[hq // n_rep], p.mean(axis=0))
+    if not per_kv_head:
+        S = S.max(axis=0, keepdims=True)
+    blk = S.reshape(S.shape[0], N, 16).sum(axis=2)
     if smooth == "always" or (smooth == "if3" and N >= 3):
-        padded = np.concatenate([[-np.inf], blk, [-np.inf]])
-        blk = np.maximum(np.maximum(padded[:-2], padded[1:-1]), padded[2:])
-    return blk
+        padded = np.concatenate([np.full((blk.shape[0], 1), -np.inf), blk, np.full((blk.shape[0], 1), -np.inf)], 1)
+        blk = np.maximum(np.maximum(padded[:, :-2], padded[:, 1:-1]), padded[:, 2:])
+    return blk if per_kv_head else blk[0]
 
 
 def topk_lowest_index(scores, k):
@@ -116,16 +121,22 @@ def writeback_source_tokens(L, sink, obs, selected, uncompressed=False):
 
 
 def writeback_pool(k_pool, v_pool, K, V, dst_pages, src_tokens):
-    """Apply a compacting writeback to copies of pool layers [N, 16, h, d]."""
+    """Apply a compacting writeback to copies of pool layers [N, 16, h, d].
+
+    src_tokens: [eff] shared by all KV heads, or [h_kv, eff] per KV head."""
     kp, vp = k_pool.copy(), v_pool.copy()
-    for p, t in enumerate(src_tokens):
-        page, slot = dst_pages[p // 16], p % 16
-        if t < 0:
-            kp[page, slot] = 0
-            vp[page, slot] = 0
-        else:
-            kp[page, slot] = K[:, t, :]
-            vp[page, slot] = V[:, t, :]
+    src = np.asarray(src_tokens)
+    if src.ndim == 1:
+        src = np.broadcast_to(src, (K.shape[0], src.shape[0]))
+    for h in range(K.shape[0]):
+        for p, t in enumerate(src[h]):
+            page, slot = dst_pages[p // 16], p % 16
+            if t < 0:
+                kp[page, slot, h] = 0
+                vp[page, slot, h] = 0
+            else:
+                kp[page, slot, h] = K[h, t, :]
+                vp[page, slot, h] = V[h, t, :]
     return kp, vp
 
 
@@ -142,3 +153,21 @@ def compress(K, V, Q, sink, obs, budget=0, ratio=0.2):
     Kf = np.where(src[None, :, None] >= 0, K[:, np.maximum(src, 0), :], 0)
     Vf = np.where(src[None, :, None] >= 0, V[:, np.maximum(src, 0), :], 0)
     return Kf, Vf, sel
+
+
+def compress_per_kv_head(K, V, Q, sink, obs, budget=0, ratio=0.2):
+    """Per-KV-head variant of compress: (K_final, V_final, selected [h_kv][k]) or (K, V, None) if skipped."""
+    h_kv, L, d = K.shape
+    if budget > 0 and L <= budget:
+        return K, V, None
+    N = int(math.ceil((L - sink - obs) / 16))
+    k = compress_k_blocks(N, sink, obs, budget, ratio)
+    scores = block_scores(K, Q, sink, obs, per_kv_head=True)
+    sels = [topk_lowest_index(scores[h], k) for h in range(h_kv)]
+    Kf = np.zeros((h_kv, sink + 16 * k + obs, d), K.dtype)
+    Vf = np.zeros_like(Kf)
+    for h in range(h_kv):
+        src = writeback_source_tokens(L, sink, obs, sels[h])
+        Kf[h] = np.where(src[:, None] >= 0, K[h, np.maximum(src, 0), :], 0)
+        Vf[h] = np.where(src[:, None] >= 0, V[h, np.maximum(src, 0), :], 0)
+    return Kf, Vf, np.stack(sels) if k > 0 else np.zeros((h_kv, 0), np.int64)

@@ -94,3 +94,26 @@ def test_topk_ties_lowest_index():
     s = np.array([1.0, 3.0, 3.0, 2.0, 3.0, 0.5])
     assert list(oc.topk_lowest_index(s, 2)) == [1, 2]
     assert list(oc.topk_lowest_index(s, 4)) == [1, 2, 3, 4]
+
+
+def test_per_kv_head_oracle_reduces_to_shared():
+    """Per-KV-head mode (no reference counterpart): with one KV head it is the
+    shared mode; with several, the shared (unsmoothed) block score bounds every
+    head's, and each head's selection is the top-k of its own row."""
+    from tests.golden.inputs import compress_case
+    K, V, Q, _ = compress_case(seed=4, h_kv=1, L=600, d=32, n_rep=4, window=8)
+    np.testing.assert_array_equal(oc.block_scores(K, Q, 16, 16, per_kv_head=True)[0], oc.block_scores(K, Q, 16, 16))
+    Kf, Vf, sel = oc.compress_per_kv_head(K, V, Q, 16, 16, ratio=0.25)
+    Kg, Vg, selg = oc.compress(K, V, Q, 16, 16, ratio=0.25)
+    np.testing.assert_array_equal(sel[0], selg)
+    np.testing.assert_array_equal(Kf, Kg)
+    K, V, Q, _ = compress_case(seed=5, h_kv=3, L=900, d=32, n_rep=2, window=8)
+    sh = oc.block_scores(K, Q, 16, 16, smooth="never")
+    ph = oc.block_scores(K, Q, 16, 16, smooth="never", per_kv_head=True)
+    assert ph.shape == (3, sh.shape[0]) and np.all(sh >= ph.max(axis=0) - 1e-15)
+    Kf, Vf, sel = oc.compress_per_kv_head(K, V, Q, 16, 16, ratio=0.25)
+    scores = oc.block_scores(K, Q, 16, 16, per_kv_head=True)
+    for h in range(3):
+        np.testing.assert_array_equal(sel[h], oc.topk_lowest_index(scores[h], sel.shape[1]))
+        src = oc.writeback_source_tokens(900, 16, 16, sel[h])
+        np.testing.assert_array_equal(Kf[h], np.where(src[:, None] >= 0, K[h, np.maximum(src, 0)], 0))

@@ -47,7 +47,14 @@ SIGNATURES = {
     "bpkv_block_score_workspace_size": (_c_sz, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "bpkv_block_score": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
                                   _c_i64, _c_i64, _c_i64, _c_i64, _c_f, _c_int, _c_int, _c_p, _c_sz, _c_p]),
+    "bpkv_block_score_per_kv_head": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                              _c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_f, _c_int, _c_int, _c_p,
+                                              _c_sz, _c_p]),
     "bpkv_topk_select": (_c_int, [_c_p, _c_int, _c_int, _c_p, _c_p]),
+    "bpkv_topk_select_batched": (_c_int, [_c_p, _c_int, _c_int, _c_int, _c_p, _c_p]),
+    "bpkv_page_compact_per_kv_head": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_i64, _c_int, _c_p, _c_int, _c_int,
+                                               _c_int, _c_int, _c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+                                               _c_int, _c_p]),
     "bpkv_page_compact": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_int, _c_p, _c_int, _c_int, _c_int,
                                    _c_int, _c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_p]),
     "bpkv_paged_prefill": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int,

@@ -31,13 +31,16 @@ def repeat_kv(x: torch.Tensor, n_rep: int) -> torch.Tensor:
 
 
 def block_scores(K: torch.Tensor, Q_obs: torch.Tensor, sink_len: int, obs_len: int,
-                 softmax_scale: float | None = None, smooth: int = SMOOTH_ALWAYS) -> torch.Tensor:
+                 softmax_scale: float | None = None, smooth: int = SMOOTH_ALWAYS,
+                 per_kv_head: bool = False) -> torch.Tensor:
     """Per-16-token-block scores of K_mid = K[:, sink:L-obs] (zero-padded to a
     multiple of 16) under the observation window Q_obs.
 
     K: [h_kv, L, d]; Q_obs: [h_q, W, d] (same dtype, bf16 or fp16, CUDA).
     Returns fp32 [N], N = ceil((L - sink - obs)/16); the math of
-    core/compress.py:116-130 / core/scheduler.py:581-591.
+    core/compress.py:116-130 / core/scheduler.py:581-591.  With per_kv_head the
+    max over q heads is taken within each KV group only and the result is
+    fp32 [h_kv, N] (this build's addition; the reference shares one score).
     """
     if K.dim() != 3 or Q_obs.dim() != 3:
         raise RuntimeError("selected_writeback_bad_score_shape")
@@ -51,29 +54,33 @@ def block_scores(K: torch.Tensor, Q_obs: torch.Tensor, sink_len: int, obs_len: i
         Q_obs = Q_obs.contiguous()
     scale = float(softmax_scale) if softmax_scale is not None else d ** -0.5
     n = math.ceil((L - sink_len - obs_len) / 16)
-    out = torch.empty(max(n, 0), dtype=torch.float32, device=K.device)
+    out = torch.empty((h_kv, max(n, 0)) if per_kv_head else (max(n, 0),), dtype=torch.float32, device=K.device)
     lib = _lib.lib()
     with torch.cuda.device(K.device):
         nbytes = lib.bpkv_block_score_workspace_size(h_q, W, L, int(sink_len), int(obs_len))
         ws = _lib.workspace(nbytes, K.device, "score")
-        rc = lib.bpkv_block_score(K.data_ptr(), Q_obs.data_ptr(), out.data_ptr(), h_kv, h_q, L, W, d, int(sink_len),
-                                  int(obs_len), K.stride(0), K.stride(1), Q_obs.stride(0), Q_obs.stride(1), scale,
-                                  int(smooth), _lib.dtype_code(K.dtype), ws.data_ptr(), ws.numel(),
-                                  _lib.stream_ptr(K.device))
+        fn = lib.bpkv_block_score_per_kv_head if per_kv_head else lib.bpkv_block_score
+        rc = fn(K.data_ptr(), Q_obs.data_ptr(), out.data_ptr(), h_kv, h_q, L, W, d, int(sink_len),
+                int(obs_len), K.stride(0), K.stride(1), Q_obs.stride(0), Q_obs.stride(1), scale,
+                int(smooth), _lib.dtype_code(K.dtype), ws.data_ptr(), ws.numel(), _lib.stream_ptr(K.device))
     _lib.check(rc, "block_score")
     return out
 
 
 def topk_blocks(scores: torch.Tensor, k: int) -> torch.Tensor:
-    """Indices (int32, ascending) of the k highest scores; ties -> lowest index."""
-    n = int(scores.numel())
+    """Indices (int32, ascending) of the k highest scores; ties -> lowest index.
+
+    scores [n] -> [k]; scores [rows, n] -> [rows, k], one selection per row
+    (the per-KV-head mode)."""
+    rows = int(scores.shape[0]) if scores.dim() == 2 else 1
+    n = int(scores.shape[-1]) if scores.dim() >= 1 else 0
     k = max(0, min(int(k), n))
-    out = torch.empty(k, dtype=torch.int32, device=scores.device)
-    if k == 0:
+    out = torch.empty((rows, k) if scores.dim() == 2 else (k,), dtype=torch.int32, device=scores.device)
+    if k == 0 or rows == 0:
         return out
     s = scores.contiguous().float()
     with torch.cuda.device(s.device):
-        rc = _lib.lib().bpkv_topk_select(s.data_ptr(), n, k, out.data_ptr(), _lib.stream_ptr(s.device))
+        rc = _lib.lib().bpkv_topk_select_batched(s.data_ptr(), n, k, rows, out.data_ptr(), _lib.stream_ptr(s.device))
     _lib.check(rc, "topk_select")
     return out
 
@@ -88,7 +95,7 @@ class BlockAlignedSnapKV:
     """
 
     def __init__(self, block_size: int = 16, sink_len: int = 64, obs_len: int = 64, retain_ratio: float = 0.20,
-                 retain_budget_tokens: int = 0):
+                 retain_budget_tokens: int = 0, per_kv_head: bool = False):
         if int(block_size) != 16:
             raise RuntimeError(f"page16_native_shape_unsupported:block_size_{block_size}")
         self.B = int(block_size)
@@ -96,6 +103,9 @@ class BlockAlignedSnapKV:
         self.Lo = int(obs_len)
         self.retain_ratio = retain_ratio
         self.retain_budget_tokens = max(0, int(retain_budget_tokens))
+        # per_kv_head (this build's addition): every KV head keeps its own top-k
+        # blocks; retained_block_idx then holds one list per KV head per batch row
+        self.per_kv_head = bool(per_kv_head)
         self.last_debug: Dict[str, Any] = {}
 
     @property
@@ -137,7 +147,8 @@ class BlockAlignedSnapKV:
         n_pages = math.ceil(eff / self.B)
         dense_pages = torch.arange(n_pages, dtype=torch.int32, device=K.device)
         for i in range(b):
-            scores = block_scores(K[i], Q_obs[i].to(K.dtype), self.Ls, self.Lo, d ** -0.5, SMOOTH_ALWAYS)
+            scores = block_scores(K[i], Q_obs[i].to(K.dtype), self.Ls, self.Lo, d ** -0.5, SMOOTH_ALWAYS,
+                                  per_kv_head=self.per_kv_head)
             sel = topk_blocks(scores, k_blocks)
             idx_all.append(sel)
             write_pages(K_out[i], V_out[i], K[i], V[i], dense_pages, sel, k_blocks, self.Ls, self.Lo, dense_out=True)
@@ -148,5 +159,6 @@ class BlockAlignedSnapKV:
             "mid_tokens_aligned": int(N * self.B), "mid_block_count": int(N),
             "retained_block_count": int(k_blocks), "effective_retained_tokens": int(eff),
             "retained_block_idx": [t.long().cpu().tolist() for t in idx_all],
+            "selection_scope": "per_kv_head" if self.per_kv_head else "shared",
         }
         return K_out, V_out

@@ -247,9 +247,11 @@ __global__ void stats_reduce_kernel(const float2* ml_part, float2* ml, int nrows
 // Block scores: a CTA of 256 threads covers kBlkPerCta blocks plus one halo
 // block on each side.  Thread = token: max over kv heads (coalesced rows of
 // headmax), 16-token sums by a fixed shuffle tree, then optional max-pool 3.
+// per_head: no max over kv heads; KV head blockIdx.y writes its own row
+// out[blockIdx.y][N].
 constexpr int kBlkPerCta = 14;  // (14 + 2) blocks x 16 tokens = 256 threads
 __global__ void __launch_bounds__(256) block_reduce_kernel(const float* headmax, float* out, int Hkv, int Tm, int N,
-                                                           int smooth) {
+                                                           int smooth, int per_head) {
   __shared__ float raw[kBlkPerCta + 2];
   const int b0 = blockIdx.x * kBlkPerCta - 1;  // first (halo) block
   const int t = threadIdx.x;
@@ -258,7 +260,11 @@ __global__ void __launch_bounds__(256) block_reduce_kernel(const float* headmax,
   float v = 0.f;
   if (blk >= 0 && blk < N) {
     float mx = -INFINITY;
-    for (int g = 0; g < Hkv; ++g) mx = fmaxf(mx, headmax[static_cast<int64_t>(g) * Tm + tok]);
+    if (per_head) {
+      mx = headmax[static_cast<int64_t>(blockIdx.y) * Tm + tok];
+    } else {
+      for (int g = 0; g < Hkv; ++g) mx = fmaxf(mx, headmax[static_cast<int64_t>(g) * Tm + tok]);
+    }
     v = mx;
   }
   for (int o = 1; o < kPage; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -273,7 +279,7 @@ __global__ void __launch_bounds__(256) block_reduce_kernel(const float* headmax,
         if (n > 0) r = fmaxf(r, raw[t]);
         if (n + 1 < N) r = fmaxf(r, raw[t + 2]);
       }
-      out[n] = r;
+      out[static_cast<int64_t>(blockIdx.y) * N + n] = r;
     }
   }
 }
@@ -320,6 +326,8 @@ __device__ int block_exclusive_scan(int local, int* wsum) {
 // order by an ordered compaction.
 __global__ void __launch_bounds__(1024) topk_select_kernel(const float* scores, int n, int k, int32_t* selected) {
   extern __shared__ __align__(128) uint8_t smem[];
+  scores += static_cast<int64_t>(blockIdx.x) * n;  // one row of a batch per CTA
+  selected += static_cast<int64_t>(blockIdx.x) * k;
   uint32_t* key = reinterpret_cast<uint32_t*>(smem);
   __shared__ int hist[256];
   __shared__ int wsum[32];
@@ -413,7 +421,8 @@ template <typename V>
 __global__ void page_compact_kernel(const uint8_t* k_src, const uint8_t* v_src, uint8_t* k_pool, uint8_t* v_pool,
                                     const int32_t* selected, int kb, const int32_t* dst_pages, int L, int sink,
                                     int obs, int eff_len, int Hkv, int row_bytes, int64_t src_sh_b,
-                                    int64_t src_st_b, int64_t page_stride_b, int64_t dst_st_b, int64_t dst_sh_b) {
+                                    int64_t src_st_b, int64_t page_stride_b, int64_t dst_st_b, int64_t dst_sh_b,
+                                    int64_t sel_stride_h) {
   const int j = blockIdx.x;  // destination page
   const bool is_v = blockIdx.y == 1;
   const uint8_t* src = is_v ? v_src : k_src;
@@ -426,7 +435,7 @@ __global__ void page_compact_kernel(const uint8_t* k_src, const uint8_t* v_src, 
     const int h = rh % Hkv, slot = rh / Hkv;
     const int p = j * kPage + slot;
     if (p >= eff_len) continue;  // slots past the compacted length stay untouched
-    const int64_t t = compact_src_token(p, L, sink, obs, kb, selected);
+    const int64_t t = compact_src_token(p, L, sink, obs, kb, selected + h * sel_stride_h);
     V val;
     if (t >= 0) {
       val = *reinterpret_cast<const V*>(src + h * src_sh_b + t * src_st_b + vi * sizeof(V));
@@ -474,7 +483,8 @@ ScoreWs score_ws(int Hq, int W, int L, int sink, int obs) {
 }
 
 template <typename T, int D>
-int launch_score(ScoreParams& p, float* out, int N, int smooth, cudaStream_t st) {
+int launch_score(ScoreParams& p, float* out, int N, int smooth, int per_head, cudaStream_t st) {
+  const dim3 rgrid((N + kBlkPerCta - 1) / kBlkPerCta, per_head ? p.Hkv : 1);
   if constexpr (D == 128) {
     ScoreTcParams t{};
     t.k = p.k;
@@ -503,7 +513,7 @@ int launch_score(ScoreParams& p, float* out, int N, int smooth, cudaStream_t st)
       stats_reduce_kernel<<<(nrows * 32 + 255) / 256, 256, 0, st>>>(p.ml_part, p.ml, nrows, t.n_chunks);
       rc = score_tc_pass(t, D, dt, 2, st);
       if (rc != BPKV_OK) return rc;
-      block_reduce_kernel<<<(N + kBlkPerCta - 1) / kBlkPerCta, 256, 0, st>>>(p.headmax, out, p.Hkv, p.Tm, N, smooth);
+      block_reduce_kernel<<<rgrid, 256, 0, st>>>(p.headmax, out, p.Hkv, p.Tm, N, smooth, per_head);
       BPKV_RETURN_LAUNCH("block_score_launch");
     }
   }
@@ -523,7 +533,7 @@ int launch_score(ScoreParams& p, float* out, int N, int smooth, cudaStream_t st)
   const int nrows = p.Hq * p.Wp;
   stats_reduce_kernel<<<(nrows * 32 + 255) / 256, 256, 0, st>>>(p.ml_part, p.ml, nrows, p.n_chunks);
   k2<<<grid, kScoreWarps * 32, smem, st>>>(p);
-  block_reduce_kernel<<<(N + kBlkPerCta - 1) / kBlkPerCta, 256, 0, st>>>(p.headmax, out, p.Hkv, p.Tm, N, smooth);
+  block_reduce_kernel<<<rgrid, 256, 0, st>>>(p.headmax, out, p.Hkv, p.Tm, N, smooth, per_head);
   BPKV_RETURN_LAUNCH("block_score_launch");
 }
 
@@ -538,11 +548,11 @@ extern "C" BPKV_API size_t bpkv_block_score_workspace_size(int num_q_heads, int 
   return score_ws(num_q_heads, window, L, sink_len, obs_len).total;
 }
 
-extern "C" BPKV_API int bpkv_block_score(const void* k, const void* q_obs, float* block_scores, int num_kv_heads,
-                                         int num_q_heads, int L, int window, int head_dim, int sink_len,
-                                         int obs_len, int64_t k_stride_h, int64_t k_stride_t,
-                                         int64_t q_stride_h, int64_t q_stride_t, float softmax_scale, int smooth,
-                                         int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+static int block_score_impl(const void* k, const void* q_obs, float* block_scores, int num_kv_heads,
+                            int num_q_heads, int L, int window, int head_dim, int sink_len, int obs_len,
+                            int64_t k_stride_h, int64_t k_stride_t, int64_t q_stride_h, int64_t q_stride_t,
+                            float softmax_scale, int smooth, int dtype, void* workspace, size_t workspace_bytes,
+                            void* stream, int per_head) {
   clear_error();
   BPKV_CHECK_ARG(num_kv_heads > 0 && num_q_heads > 0 && num_q_heads % num_kv_heads == 0,
                  "selected_writeback_bad_score_shape:gqa");
@@ -592,10 +602,10 @@ extern "C" BPKV_API int bpkv_block_score(const void* k, const void* q_obs, float
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 #define BPKV_SCORE(TY)                                                      \
   switch (head_dim) {                                                       \
-    case 32: return launch_score<TY, 32>(p, block_scores, N, smooth, st);   \
-    case 64: return launch_score<TY, 64>(p, block_scores, N, smooth, st);   \
-    case 128: return launch_score<TY, 128>(p, block_scores, N, smooth, st); \
-    default: return launch_score<TY, 256>(p, block_scores, N, smooth, st);  \
+    case 32: return launch_score<TY, 32>(p, block_scores, N, smooth, per_head, st);   \
+    case 64: return launch_score<TY, 64>(p, block_scores, N, smooth, per_head, st);   \
+    case 128: return launch_score<TY, 128>(p, block_scores, N, smooth, per_head, st); \
+    default: return launch_score<TY, 256>(p, block_scores, N, smooth, per_head, st);  \
   }
   if (dtype == BPKV_BF16) {
     BPKV_SCORE(__nv_bfloat16)
@@ -605,8 +615,31 @@ extern "C" BPKV_API int bpkv_block_score(const void* k, const void* q_obs, float
 #undef BPKV_SCORE
 }
 
-extern "C" BPKV_API int bpkv_topk_select(const float* scores, int n, int k, int32_t* selected, void* stream) {
+extern "C" BPKV_API int bpkv_block_score(const void* k, const void* q_obs, float* block_scores, int num_kv_heads,
+                                         int num_q_heads, int L, int window, int head_dim, int sink_len,
+                                         int obs_len, int64_t k_stride_h, int64_t k_stride_t,
+                                         int64_t q_stride_h, int64_t q_stride_t, float softmax_scale, int smooth,
+                                         int dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  return block_score_impl(k, q_obs, block_scores, num_kv_heads, num_q_heads, L, window, head_dim, sink_len, obs_len,
+                          k_stride_h, k_stride_t, q_stride_h, q_stride_t, softmax_scale, smooth, dtype, workspace,
+                          workspace_bytes, stream, 0);
+}
+
+extern "C" BPKV_API int bpkv_block_score_per_kv_head(const void* k, const void* q_obs, float* block_scores,
+                                                     int num_kv_heads, int num_q_heads, int L, int window,
+                                                     int head_dim, int sink_len, int obs_len, int64_t k_stride_h,
+                                                     int64_t k_stride_t, int64_t q_stride_h, int64_t q_stride_t,
+                                                     float softmax_scale, int smooth, int dtype, void* workspace,
+                                                     size_t workspace_bytes, void* stream) {
+  return block_score_impl(k, q_obs, block_scores, num_kv_heads, num_q_heads, L, window, head_dim, sink_len, obs_len,
+                          k_stride_h, k_stride_t, q_stride_h, q_stride_t, softmax_scale, smooth, dtype, workspace,
+                          workspace_bytes, stream, 1);
+}
+
+extern "C" BPKV_API int bpkv_topk_select_batched(const float* scores, int n, int k, int batch, int32_t* selected,
+                                                 void* stream) {
   clear_error();
+  BPKV_CHECK_ARG(batch >= 0, "selected_writeback_topk_shape:batch_%d", batch);
   BPKV_CHECK_ARG(n >= 0 && k >= 0 && k <= n, "selected_writeback_topk_shape:n_%d_k_%d", n, k);
   BPKV_CHECK_ARG(n <= 49152, "selected_writeback_topk_shape:n_%d_exceeds_49152", n);
   if (k == 0) return BPKV_OK;
@@ -620,15 +653,20 @@ extern "C" BPKV_API int bpkv_topk_select(const float* scores, int n, int k, int3
                          static_cast<int>(sizeof(uint32_t) * 49152));
     raised[dev] = true;
   }
-  topk_select_kernel<<<1, 1024, smem, static_cast<cudaStream_t>(stream)>>>(scores, n, k, selected);
+  if (batch == 0) return BPKV_OK;
+  topk_select_kernel<<<batch, 1024, smem, static_cast<cudaStream_t>(stream)>>>(scores, n, k, selected);
   BPKV_RETURN_LAUNCH("topk_select_launch");
 }
 
-extern "C" BPKV_API int bpkv_page_compact(const void* k_src, const void* v_src, void* k_pool, void* v_pool,
-                                          const int32_t* selected, int k_blocks, const int32_t* dst_pages, int L,
-                                          int sink_len, int obs_len, int num_kv_heads, int head_dim,
-                                          int64_t src_stride_h, int64_t src_stride_t, int64_t page_stride,
-                                          int64_t dst_stride_t, int64_t dst_stride_h, int dtype, void* stream) {
+extern "C" BPKV_API int bpkv_topk_select(const float* scores, int n, int k, int32_t* selected, void* stream) {
+  return bpkv_topk_select_batched(scores, n, k, 1, selected, stream);
+}
+
+static int page_compact_impl(const void* k_src, const void* v_src, void* k_pool, void* v_pool,
+                             const int32_t* selected, int64_t sel_stride_h, int k_blocks, const int32_t* dst_pages,
+                             int L, int sink_len, int obs_len, int num_kv_heads, int head_dim, int64_t src_stride_h,
+                             int64_t src_stride_t, int64_t page_stride, int64_t dst_stride_t, int64_t dst_stride_h,
+                             int dtype, void* stream) {
   clear_error();
   BPKV_CHECK_ARG(L > 0 && num_kv_heads > 0 && head_dim > 0 && sink_len >= 0 && obs_len >= 0,
                  "selected_writeback_shape:empty");
@@ -652,14 +690,45 @@ extern "C" BPKV_API int bpkv_page_compact(const void* k_src, const void* v_src, 
   uint8_t *kp = static_cast<uint8_t*>(k_pool), *vp = static_cast<uint8_t*>(v_pool);
   if (v16)
     page_compact_kernel<uint4><<<grid, 256, 0, st>>>(ks, vs, kp, vp, selected, k_blocks, dst_pages, L, sink_len,
-                                                     obs_len, eff_len, num_kv_heads, row_bytes, sh, stt, ps, dt, dh);
+                                                     obs_len, eff_len, num_kv_heads, row_bytes, sh, stt, ps, dt, dh,
+        sel_stride_h);
   else if (esz == 4)
     page_compact_kernel<uint32_t><<<grid, 256, 0, st>>>(ks, vs, kp, vp, selected, k_blocks, dst_pages, L, sink_len,
-                                                        obs_len, eff_len, num_kv_heads, row_bytes, sh, stt, ps, dt, dh);
+                                                        obs_len, eff_len, num_kv_heads, row_bytes, sh, stt, ps, dt, dh,
+        sel_stride_h);
   else
     page_compact_kernel<uint16_t><<<grid, 256, 0, st>>>(ks, vs, kp, vp, selected, k_blocks, dst_pages, L, sink_len,
-                                                        obs_len, eff_len, num_kv_heads, row_bytes, sh, stt, ps, dt, dh);
+                                                        obs_len, eff_len, num_kv_heads, row_bytes, sh, stt, ps, dt, dh,
+        sel_stride_h);
   BPKV_RETURN_LAUNCH("page_compact_launch");
+}
+
+extern "C" BPKV_API int bpkv_page_compact(const void* k_src, const void* v_src, void* k_pool, void* v_pool,
+                                          const int32_t* selected, int k_blocks, const int32_t* dst_pages, int L,
+                                          int sink_len, int obs_len, int num_kv_heads, int head_dim,
+                                          int64_t src_stride_h, int64_t src_stride_t, int64_t page_stride,
+                                          int64_t dst_stride_t, int64_t dst_stride_h, int dtype, void* stream) {
+  return page_compact_impl(k_src, v_src, k_pool, v_pool, selected, 0, k_blocks, dst_pages, L, sink_len, obs_len,
+                           num_kv_heads, head_dim, src_stride_h, src_stride_t, page_stride, dst_stride_t,
+                           dst_stride_h, dtype, stream);
+}
+
+extern "C" BPKV_API int bpkv_page_compact_per_kv_head(const void* k_src, const void* v_src, void* k_pool,
+                                                      void* v_pool, const int32_t* selected,
+                                                      int64_t selected_stride_h, int k_blocks,
+                                                      const int32_t* dst_pages, int L, int sink_len, int obs_len,
+                                                      int num_kv_heads, int head_dim, int64_t src_stride_h,
+                                                      int64_t src_stride_t, int64_t page_stride,
+                                                      int64_t dst_stride_t, int64_t dst_stride_h, int dtype,
+                                                      void* stream) {
+  if (k_blocks > 0 && selected_stride_h < k_blocks) {
+    clear_error();
+    set_error("selected_writeback_shape:selected_stride_%lld", static_cast<long long>(selected_stride_h));
+    return BPKV_ERR_SHAPE;
+  }
+  return page_compact_impl(k_src, v_src, k_pool, v_pool, selected, selected_stride_h, k_blocks, dst_pages, L,
+                           sink_len, obs_len, num_kv_heads, head_dim, src_stride_h, src_stride_t, page_stride,
+                           dst_stride_t, dst_stride_h, dtype, stream);
 }
 
 static int page_move(const void* src, void* dst, const int32_t* ids, int n_pages, int64_t page_elems,

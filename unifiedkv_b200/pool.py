@@ -174,7 +174,8 @@ def write_pages(k_dst: torch.Tensor, v_dst: torch.Tensor, K: torch.Tensor, V: to
 
     k_dst/v_dst: a pool layer view [N, 16, h_kv, d] (or, with dense_out, a dense
     [h_kv, eff_len, d] tensor); K, V: [h_kv, L, d] sources; dst_pages: list or
-    int32 device tensor; selected: int32 device tensor of k_blocks mid blocks
+    int32 device tensor; selected: int32 device tensor of k_blocks mid blocks,
+    or [h_kv, k_blocks] with each KV head's own blocks (per-KV-head selection)
     (k_blocks < 0 = uncompressed copy of the first ``length`` tokens).
     """
     h_kv, L, d = [int(x) for x in K.shape]
@@ -193,8 +194,16 @@ def write_pages(k_dst: torch.Tensor, v_dst: torch.Tensor, K: torch.Tensor, V: to
     if k_dst.dtype != K.dtype:
         raise RuntimeError("selected_writeback_shape:dtype_mismatch")
     with torch.cuda.device(K.device):
-        rc = _lib.lib().bpkv_page_compact(
-            K.data_ptr(), V.data_ptr(), k_dst.data_ptr(), v_dst.data_ptr(), _lib.ptr(selected), int(k_blocks),
-            dst_pages.data_ptr(), L, int(sink), int(obs), h_kv, d, K.stride(0), K.stride(1), ps, st, sh,
-            _lib.dtype_code(K.dtype), _lib.stream_ptr(K.device))
+        if selected is not None and selected.dim() == 2:
+            if int(selected.shape[0]) != h_kv or selected.stride(1) != 1:
+                raise RuntimeError("selected_writeback_shape:per_kv_head_selected")
+            rc = _lib.lib().bpkv_page_compact_per_kv_head(
+                K.data_ptr(), V.data_ptr(), k_dst.data_ptr(), v_dst.data_ptr(), selected.data_ptr(),
+                selected.stride(0), int(k_blocks), dst_pages.data_ptr(), L, int(sink), int(obs), h_kv, d,
+                K.stride(0), K.stride(1), ps, st, sh, _lib.dtype_code(K.dtype), _lib.stream_ptr(K.device))
+        else:
+            rc = _lib.lib().bpkv_page_compact(
+                K.data_ptr(), V.data_ptr(), k_dst.data_ptr(), v_dst.data_ptr(), _lib.ptr(selected), int(k_blocks),
+                dst_pages.data_ptr(), L, int(sink), int(obs), h_kv, d, K.stride(0), K.stride(1), ps, st, sh,
+                _lib.dtype_code(K.dtype), _lib.stream_ptr(K.device))
     _lib.check(rc, "selected_writeback")

@@ -70,7 +70,7 @@ class SelectedWritebackOps:
             return torch.empty((0,), dtype=torch.float32, device=dev)
         self.score_full_attention_materialized = 0
         return block_scores(K, Q_obs, int(self.snapkv.Ls), int(self.snapkv.Lo), float(self.head_dim) ** -0.5,
-                            SMOOTH_IF_3)
+                            SMOOTH_IF_3, per_kv_head=bool(getattr(self.snapkv, "per_kv_head", False)))
 
     def _select_layer_device(self, layer_id: int, seq_id: int, raw, k_blocks: int) -> torch.Tensor:
         Q_full = self.q_cache[layer_id].get(seq_id)
@@ -78,7 +78,8 @@ class SelectedWritebackOps:
             raise RuntimeError(f"selected_writeback_missing_q seq={seq_id} layer={layer_id}")
         Q_obs = Q_full[:, -int(self.snapkv.Lo):, :]
         score = self._score_layer_blocks_for_selection(raw[0], Q_obs)
-        return topk_blocks(score, max(0, min(int(k_blocks), int(score.numel()))))
+        n = int(score.shape[-1]) if score.dim() >= 1 else 0
+        return topk_blocks(score, max(0, min(int(k_blocks), n)))
 
     def _compute_per_layer_selected_blocks(self, seq_id: int, raw_by_layer) -> Tuple[Dict[int, List[int]], int, int, str]:
         first = next((kv for kv in raw_by_layer.values() if kv is not None), None)
@@ -97,7 +98,7 @@ class SelectedWritebackOps:
                     raise RuntimeError(f"selected_writeback_missing_raw seq={seq_id} layer={layer_id}")
                 dev_sel.append(self._select_layer_device(layer_id, seq_id, raw, k_blocks))
             host = [t.cpu().tolist() for t in dev_sel]  # one sync point per sequence
-            selected = {int(l): [int(x) for x in host[l]] for l in range(self.num_layers)}
+            selected = {int(l): host[l] for l in range(self.num_layers)}  # [k] or per KV head [h_kv][k]
         self._record_selection_debug(L, k_blocks, effective_len, mode, selected)
         return selected, int(effective_len), int(L), str(mode)
 
@@ -114,6 +115,7 @@ class SelectedWritebackOps:
             "effective_retained_tokens": int(effective_len),
             "retained_block_idx": [selected.get(int(l), []) for l in range(self.num_layers)],
             "shared_block_selection": False, "selection_granularity": "per_layer_block_topk",
+            "selection_scope": "per_kv_head" if getattr(self.snapkv, "per_kv_head", False) else "shared",
             "compression_skipped": mode if mode in ("input_le_budget", "too_short") else "",
         }
 
@@ -170,11 +172,10 @@ class SelectedWritebackOps:
             write_pages(kc, vc, K, V, block_ids, None, -1, 0, 0, length=int(effective_len))
             return anchor
         if torch.is_tensor(selected_mid_blocks):
-            sel = selected_mid_blocks.to(dev, torch.int32)
-            k = int(sel.numel())
-        else:
-            k = len(selected_mid_blocks)
-            sel = torch.tensor([int(x) for x in selected_mid_blocks], dtype=torch.int32).to(dev, non_blocking=True)
+            sel = selected_mid_blocks.to(dev, torch.int32).contiguous()
+        else:  # [k] shared, or [h_kv][k] per KV head
+            sel = torch.tensor(selected_mid_blocks, dtype=torch.int32).to(dev, non_blocking=True)
+        k = int(sel.shape[-1]) if sel.dim() >= 1 else 0
         if Ls + 16 * k + Lo != int(effective_len):
             raise RuntimeError(f"selected_writeback_len_mismatch got={Ls + 16 * k + Lo} expected={effective_len}")
         write_pages(kc, vc, K, V, block_ids, sel, k, Ls, Lo)
@@ -231,7 +232,7 @@ class SelectedWritebackOps:
             for layer_id in range(self.num_layers):
                 dev_sel[layer_id] = self._select_layer_device(layer_id, seq_id, raw_by_layer[layer_id], k_blocks)
         self._selected_writeback_transaction(seq_id, raw_by_layer, dev_sel, eff, L, mode)
-        host = {l: [int(x) for x in t.cpu().tolist()] for l, t in dev_sel.items()}
+        host = {l: t.cpu().tolist() for l, t in dev_sel.items()}
         selected = {l: host.get(l, []) for l in range(self.num_layers)}
         self._record_selection_debug(L, k_blocks, eff, mode, selected)
         return self.page_table[(int(seq_id), 0)].block_ids, selected, eff
@@ -242,14 +243,15 @@ class SelectionEngine(SelectedWritebackOps):
     compressor settings, cached window queries and a page table."""
 
     def __init__(self, pool: PagedKVPool, num_q_heads: int, sink_len: int = 16, obs_len: int = 16,
-                 retain_ratio: float = 0.2, retain_budget_tokens: int = 0):
+                 retain_ratio: float = 0.2, retain_budget_tokens: int = 0, per_kv_head: bool = False):
         self.pool = pool
         self.num_layers = pool.num_layers
         self.num_kv_heads = pool.num_kv_heads
         self.head_dim = pool.head_dim
         self.num_q_heads = int(num_q_heads)
         self.n_rep = self.num_q_heads // self.num_kv_heads
-        self.snapkv = BlockAlignedSnapKV(16, sink_len, obs_len, retain_ratio, retain_budget_tokens)
+        self.snapkv = BlockAlignedSnapKV(16, sink_len, obs_len, retain_ratio, retain_budget_tokens,
+                                         per_kv_head=per_kv_head)
         self.q_cache: List[Dict[int, torch.Tensor]] = [dict() for _ in range(self.num_layers)]
         self.page_table: Dict[Tuple[int, int], BlockTableEntry] = {}
         self.writeback_transaction_rollbacks = 0

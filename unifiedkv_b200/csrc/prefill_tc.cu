@@ -526,9 +526,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           }
         }
         // P_g(it) over this chunk of S_g: token pair per 32-bit column, hi parts then lo parts
-        tc::tmem_st16(ts + c0, hi);
-        if (kBf16) tc::tmem_st16(ts + c0 + 16, lo);
+        tc::tmem_st16_nowait(ts + c0, hi);
+        if (kBf16) tc::tmem_st16_nowait(ts + c0 + 16, lo);
       }
+      tc::tmem_st_wait();  // all P stores of this tile complete before the arrival below
       BPKV_MARK(5);
       {
         float sa, sb;

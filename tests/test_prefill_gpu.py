@@ -132,3 +132,61 @@ def test_paged_prefill_stale_nan_rows(cuda):
         ref = chunk_attention(qn[qo:qo + chunk[b]], kb, vb)
         assert _err(out[qo:qo + chunk[b]], ref, dtype) < 2e-3
         qo += chunk[b]
+
+
+def _paged_case(cuda, hq, hkv, d, dtype, past, chunk, seed):
+    """Random pool pages in a shuffled table, q for the chunks; returns what the oracle needs."""
+    rng = np.random.default_rng(seed)
+    B = len(past)
+    totals = [p + c for p, c in zip(past, chunk)]
+    need = [math.ceil(t / 16) for t in totals]
+    n_pages = sum(need) + 3
+    perm = rng.permutation(n_pages)
+    g = torch.Generator(device=cuda).manual_seed(seed)
+    kc = torch.randn(n_pages, 16, hkv, d, generator=g, device=cuda).to(dtype)
+    vc = torch.randn(n_pages, 16, hkv, d, generator=g, device=cuda).to(dtype)
+    bt = np.zeros((B, max(need)), np.int32)
+    off = 0
+    for b in range(B):
+        bt[b, :need[b]] = perm[off:off + need[b]]
+        off += need[b]
+    q = torch.randn(sum(chunk), hq, d, generator=g, device=cuda).to(dtype)
+    return kc, vc, bt, q, totals, need
+
+
+def _check_paged(cuda, out, kc, vc, bt, q, totals, need, chunk, hkv, d, dtype):
+    out = out.float().cpu().numpy()
+    qn = q.float().cpu().numpy()
+    qo = 0
+    for b in range(len(chunk)):
+        pages = torch.from_numpy(bt[b, :need[b]].astype(np.int64)).to(cuda)
+        kb = kc.index_select(0, pages).reshape(-1, hkv, d)[:totals[b]].float().cpu().numpy()
+        vb = vc.index_select(0, pages).reshape(-1, hkv, d)[:totals[b]].float().cpu().numpy()
+        ref = chunk_attention(qn[qo:qo + chunk[b]], kb, vb)
+        assert _err(out[qo:qo + chunk[b]], ref, dtype) < 2e-3
+        qo += chunk[b]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hq,hkv", [(8, 8), (16, 8), (64, 8)])
+def test_paged_chunk_prefill_gqa_groups(cuda, dtype, hq, hkv):
+    """n_rep 1, 2 and 8: 128, 64 and 16 query tokens per Q tile of the tcgen05 kernel,
+    with chunks that end inside a tile and requests whose pasts end inside a page."""
+    from unifiedkv_b200.chunked_prefill import paged_chunk_prefill
+    d = 128
+    past, chunk = [0, 33, 700, 5], [300, 129, 64, 1]
+    kc, vc, bt, q, totals, need = _paged_case(cuda, hq, hkv, d, dtype, past, chunk, seed=hq)
+    out = paged_chunk_prefill(q, kc, vc, torch.from_numpy(bt).to(cuda), past, chunk, d ** -0.5, hq // hkv)
+    _check_paged(cuda, out, kc, vc, bt, q, totals, need, chunk, hkv, d, dtype)
+
+
+def test_paged_chunk_prefill_past_beyond_staged_table(cuda):
+    """A past of 33 000 tokens spans more than the 2048 block-table entries the kernel
+    stages in shared memory; the later pages come straight from the table in HBM."""
+    from unifiedkv_b200.chunked_prefill import paged_chunk_prefill
+    hq, hkv, d, dtype = 32, 8, 128, torch.bfloat16
+    past, chunk = [33000], [70]
+    kc, vc, bt, q, totals, need = _paged_case(cuda, hq, hkv, d, dtype, past, chunk, seed=77)
+    assert need[0] > 2048
+    out = paged_chunk_prefill(q, kc, vc, torch.from_numpy(bt).to(cuda), past, chunk, d ** -0.5, hq // hkv)
+    _check_paged(cuda, out, kc, vc, bt, q, totals, need, chunk, hkv, d, dtype)

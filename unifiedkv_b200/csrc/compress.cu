@@ -250,8 +250,8 @@ __global__ void stats_reduce_kernel(const float2* ml_part, float2* ml, int nrows
 // per_head: no max over kv heads; KV head blockIdx.y writes its own row
 // out[blockIdx.y][N].
 constexpr int kBlkPerCta = 14;  // (14 + 2) blocks x 16 tokens = 256 threads
-__global__ void __launch_bounds__(256) block_reduce_kernel(const float* headmax, float* out, int Hkv, int Tm, int N,
-                                                           int smooth, int per_head) {
+__global__ void __launch_bounds__(256) block_reduce_kernel(const float* headmax, float* out, int Hkv, int slots,
+                                                           int Tm, int N, int smooth, int per_head) {
   __shared__ float raw[kBlkPerCta + 2];
   const int b0 = blockIdx.x * kBlkPerCta - 1;  // first (halo) block
   const int t = threadIdx.x;
@@ -260,11 +260,10 @@ __global__ void __launch_bounds__(256) block_reduce_kernel(const float* headmax,
   float v = 0.f;
   if (blk >= 0 && blk < N) {
     float mx = -INFINITY;
-    if (per_head) {
-      mx = headmax[static_cast<int64_t>(blockIdx.y) * Tm + tok];
-    } else {
-      for (int g = 0; g < Hkv; ++g) mx = fmaxf(mx, headmax[static_cast<int64_t>(g) * Tm + tok]);
-    }
+    // rows g*slots .. g*slots+slots-1 belong to KV group g
+    const int r0 = per_head ? static_cast<int>(blockIdx.y) * slots : 0;
+    const int r1 = per_head ? r0 + slots : Hkv * slots;
+    for (int r = r0; r < r1; ++r) mx = fmaxf(mx, headmax[static_cast<int64_t>(r) * Tm + tok]);
     v = mx;
   }
   for (int o = 1; o < kPage; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -473,7 +472,7 @@ ScoreWs score_ws(int Hq, int W, int L, int sink, int obs) {
   const int Tm = N * kPage;
   const int Wp = (W + 15) / 16 * 16;
   const int n_chunks = (Tm + kTileTok * kChunkTiles - 1) / (kTileTok * kChunkTiles);
-  const int Hkv_max = Hq;  // upper bound for headmax rows
+  const int Hkv_max = Hq;  // upper bound for headmax rows (KV groups x head slots <= q heads)
   ScoreWs w;
   w.ml_part = 0;
   w.ml = align_up(sizeof(float2) * static_cast<size_t>(Hq) * Wp * n_chunks, 256);
@@ -513,7 +512,7 @@ int launch_score(ScoreParams& p, float* out, int N, int smooth, int per_head, cu
       stats_reduce_kernel<<<(nrows * 32 + 255) / 256, 256, 0, st>>>(p.ml_part, p.ml, nrows, t.n_chunks);
       rc = score_tc_pass(t, D, dt, 2, st);
       if (rc != BPKV_OK) return rc;
-      block_reduce_kernel<<<rgrid, 256, 0, st>>>(p.headmax, out, p.Hkv, p.Tm, N, smooth, per_head);
+      block_reduce_kernel<<<rgrid, 256, 0, st>>>(p.headmax, out, p.Hkv, t.hm_slots, p.Tm, N, smooth, per_head);
       BPKV_RETURN_LAUNCH("block_score_launch");
     }
   }
@@ -533,7 +532,7 @@ int launch_score(ScoreParams& p, float* out, int N, int smooth, int per_head, cu
   const int nrows = p.Hq * p.Wp;
   stats_reduce_kernel<<<(nrows * 32 + 255) / 256, 256, 0, st>>>(p.ml_part, p.ml, nrows, p.n_chunks);
   k2<<<grid, kScoreWarps * 32, smem, st>>>(p);
-  block_reduce_kernel<<<rgrid, 256, 0, st>>>(p.headmax, out, p.Hkv, p.Tm, N, smooth, per_head);
+  block_reduce_kernel<<<rgrid, 256, 0, st>>>(p.headmax, out, p.Hkv, 1, p.Tm, N, smooth, per_head);
   BPKV_RETURN_LAUNCH("block_score_launch");
 }
 

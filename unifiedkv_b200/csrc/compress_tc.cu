@@ -37,8 +37,8 @@ constexpr int kNK = 3;                         // K ring depth
 constexpr int kComputeWarps = 16;
 constexpr int kLoadWarp = kComputeWarps, kMmaWarp = kComputeWarps + 1;
 constexpr int kThreads = (kComputeWarps + 2) * 32;
-constexpr int kSmem = kQBytes + kNK * kKBytes + 1024 /*align*/ + 256 /*barriers*/ + kRowsMax * 4 /*row offsets*/ +
-                      2 * 4 * kTok * 4 /*head-max exchange*/;
+constexpr int kSmem = kQBytes + kNK * kKBytes + 1024 /*align*/ + 256 /*barriers*/ +
+                      2 * kRowsMax * 2 * 4 /*pass 1: (m, l) merge of the row halves; pass 2: row offsets*/;
 // every kEmu1-th / kEmu2-th exponential pair of pass 1 / pass 2 goes to the FMA pipe
 constexpr int kEmu1 = 8, kEmu2 = 8;
 
@@ -116,7 +116,6 @@ __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_cons
   // bars: k_full[kNK], k_free[kNK], s_full[2], s_free[2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kNK + 4);
   float* s_off = reinterpret_cast<float*>(bars + 32);   // PASS 1: [2][kRowsMax] (m, l) merge; PASS 2: per row -(m + log2 l)
-  float* s_hm = s_off + kRowsMax;                        // PASS 2: [2 buffers][4 head slots][kTok]
   const int g = blockIdx.y, chunk = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rows = p.n_rep * p.Wp;
@@ -337,15 +336,10 @@ __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_cons
           }
         }
         release(j);
-        // max over the four head slots
-        float* hm = s_hm + (j & 1) * 4 * kTok;
-        hm[hs * kTok + tt] = best;
-        asm volatile("bar.sync 1, %0;\n" ::"n"(32 * kComputeWarps) : "memory");
+        // each head slot writes its own row; the max over the slots is taken by the block reduction
         const int t = (tile0 + j) * kTok + tt;
-        if (hs == 0 && t < p.Tm)
-          p.headmax[static_cast<int64_t>(g) * p.Tm + t] =
-              failed ? __int_as_float(0x7fc00000)
-                     : fmaxf(fmaxf(hm[tt], hm[kTok + tt]), fmaxf(hm[2 * kTok + tt], hm[3 * kTok + tt]));
+        if (hs < p.hm_slots && t < p.Tm)
+          p.headmax[static_cast<int64_t>(g * p.hm_slots + hs) * p.Tm + t] = failed ? __int_as_float(0x7fc00000) : best;
       }
     }
   }
@@ -384,6 +378,7 @@ int score_tc_pass(ScoreTcParams& p, int head_dim, int dtype, int pass, cudaStrea
   EncodeTiledFn enc = encode_fn();
   if (enc == nullptr) return BPKV_ERR_UNSUPPORTED;
   const int ntiles = (p.Tm + kTok - 1) / kTok;
+  p.hm_slots = min(4, p.n_rep);  // pass 2's head slots (headmax rows per KV group)
   if (pass == 1) {
     // about one CTA per SM: split each group's tiles into contiguous ranges (p.n_chunks
     // arrives as the workspace's capacity of partial-stat slots per row)

@@ -13,11 +13,12 @@ struct ScoreTcParams {
   int Hkv, n_rep, W, Wp, Lm, Tm, sink;
   int n_chunks;         // in: partial-stat slots per window row in the workspace; out: ranges per KV group
   int tiles_per_chunk;  // out (pass 1): 128-token K tiles per range
+  int hm_slots;         // out (pass 2): headmax rows per KV group (one per head slot; max taken later)
   int64_t k_sh, k_st, q_sh, q_st;
   float scale_log2;
   float2* ml_part;   // [Hq*Wp][n_chunks] (m in log2 units, l)
   const float2* ml;  // [Hq*Wp]
-  float* headmax;    // [Hkv][Tm]
+  float* headmax;    // [Hkv * hm_slots][Tm]
 };
 
 // Pass 1 (row statistics) or pass 2 (per-token head max) on tcgen05 when the shape

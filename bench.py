@@ -518,17 +518,23 @@ def run_longseq(args, rank, world, local_rank):
     lens = torch.tensor([local_range_lens(L, s, e)], dtype=torch.int32, device=dev)
     from unifiedkv_b200.page16_native import page16_decode_attention
 
+    exchange = getattr(args, "exchange", "p2p")
+    peer = None
+    if world > 1 and exchange == "p2p":
+        from unifiedkv_b200.multi_gpu import PeerMerge
+        peer = PeerMerge(rows=HQ, head_dim=D, device=dev)
+
     def step():
         for l in range(layers):
             if world > 1:
-                split_kv_decode(qs[l], kp[l], vp[l], bt, lens, D ** -0.5, HQ // HKV)
+                split_kv_decode(qs[l], kp[l], vp[l], bt, lens, D ** -0.5, HQ // HKV, peer=peer)
             else:
                 page16_decode_attention(qs[l], kp[l], vp[l], bt, lens, softmax_scale=D ** -0.5, n_rep=HQ // HKV)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    # the 32-layer step (decode, NCCL all-gather, merge) is captured once in a CUDA
-    # graph: per-layer work is ~40-80 us, comparable to the Python launch cost
+    # the 32-layer step (decode, exchange, merge) is captured once in a CUDA graph:
+    # per-layer work is ~10-90 us, comparable to the Python launch cost
     graph = None
     try:
         graph = torch.cuda.CUDAGraph()
@@ -550,10 +556,14 @@ def run_longseq(args, rank, world, local_rank):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
+    if peer is not None:
+        peer.check()
     if world > 1:
         t = torch.tensor([ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+    if peer is not None:
+        peer.close()  # collective; the captured graph is not replayed after this
     if rank != 0:
         return
     bytes_step = L * KV_BYTES_PER_TOKEN * layers
@@ -564,7 +574,9 @@ def run_longseq(args, rank, world, local_rank):
         "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "strong", "dtype": "bf16", "data": "synthetic N(0,1) K/V",
         "config": {"workload": "B=1, 131072 tokens (8192 pages) split over GPUs, 32 layers, 32q/8kv, d128",
-                   "parallelism": f"split-KV x{world} + NCCL all-gather of (out, lse)",
+                   "parallelism": f"split-KV x{world}" + ("" if world == 1 else (
+                       " + (out, lse) stored into peers' buffers over NVLink, flag-synchronised merge kernel"
+                       if peer is not None else " + NCCL all-gather of (out, lse)")),
                    "launch": "CUDA graph of the 32-layer step" if graph is not None else "eager"},
         "ms_per_layer": round(ms / layers, 4), "tokens_per_s": round(1000.0 / ms, 2),
         "hbm_frac_of_measured_per_gpu": round(gbs / world / hbm, 4),
@@ -688,6 +700,8 @@ def main():
     ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "compress", "longseq", "mixed"],
                     help="decode = headline config 2; the others print their own metric line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="longseq workload at N>1: partial exchange over NVLink peer memory or NCCL all-gather")
     ap.add_argument("--per-kv-head", action="store_true",
                     help="compress workload: per-KV-head block selection instead of the shared one")
     ap.add_argument("--profile-small", action="store_true",

@@ -147,6 +147,37 @@ BPKV_API int bpkv_lse_combine(const float* part_out, const float* part_lse, void
                      int num_parts, int rows, int head_dim, int out_dtype, void* stream);
 
 /* ------------------------------------------------------------------------ *
+ * Split-KV merge over NVLink peer memory.
+ * Replaces the all-gather of packed (out, lse) partials + merge of the
+ * long-sequence decode (the reference mirrors KV heads between GPUs instead,
+ * core/multi_gpu.py:7-123; this build splits one sequence's pages across
+ * GPUs).  Setup, once per process group and shape:
+ *   bytes = bpkv_peer_exchange_bytes(world, rows, head_dim);
+ *   bpkv_peer_buffer_alloc(bytes, &own, handle)   (zeroed; 64-byte CUDA IPC handle)
+ *   exchange the handles between the processes, then on every rank
+ *   bpkv_peer_buffer_open(handle_of_rank_r, &bufs[r]) for r != rank (bufs[rank] = own).
+ * Per call (every rank makes the same sequence of calls; the call number is
+ * kept in the buffer itself, so the two kernels of a call can be captured in a
+ * CUDA graph and replayed):
+ *   bpkv_split_kv_merge_p2p: this rank's partial part_out [rows, head_dim]
+ *   (dtype) with natural-log part_lse [rows] is stored into every rank's
+ *   buffer over NVLink, a flag per rank marks it landed, then every rank
+ *   waits for all flags of this epoch and writes the merged out [rows,
+ *   head_dim] (and lse_out [rows] if not null).  A wait gives up after
+ *   max_polls polls (~64 ns apart): *status is set to 1 and the rows are NaN.
+ * Teardown: bpkv_peer_buffer_close(bufs[r]) for r != rank, after a barrier
+ * bpkv_peer_buffer_free(own).  world <= 8; head_dim % 4 == 0.  No multicast.
+ * ------------------------------------------------------------------------ */
+BPKV_API size_t bpkv_peer_exchange_bytes(int world, int rows, int head_dim);
+BPKV_API int bpkv_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+BPKV_API int bpkv_peer_buffer_open(const void* ipc_handle, void** ptr);
+BPKV_API int bpkv_peer_buffer_close(void* ptr);
+BPKV_API int bpkv_peer_buffer_free(void* ptr);
+BPKV_API int bpkv_split_kv_merge_p2p(const void* part_out, const float* part_lse, void* const* peer_bufs,
+                     int rank, int world, int rows, int head_dim, uint32_t max_polls,
+                     void* out, float* lse_out, int* status, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------ *
  * Decode-token append: writes this step's k/v into the paged pool at slot
  * (block_table[b, old_len/16], old_len % 16).
  * Replaces the indexed scatter of core/scheduler.py:398-408

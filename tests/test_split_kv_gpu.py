@@ -93,3 +93,121 @@ def test_split_kv_nccl_two_ranks(cuda):
         p.join(timeout=60)
         assert p.exitcode == 0
     assert all(err < 2e-3 for _, err in res), res
+
+
+# ---- NVLink peer-memory exchange (bpkv_split_kv_merge_p2p) ----
+
+def _p2p_call(L, part, lse, bufs, rank, world, out, lse_out, status, max_polls):
+    import ctypes
+    from unifiedkv_b200 import _lib
+    arr = (ctypes.c_void_p * world)(*bufs)
+    rc = L.bpkv_split_kv_merge_p2p(part.data_ptr(), lse.data_ptr(), arr, rank, world, int(part.shape[0]),
+                                   int(part.shape[1]), max_polls, out.data_ptr(), _lib.ptr(lse_out),
+                                   status.data_ptr(), _lib.dtype_code(part.dtype), _lib.stream_ptr(part.device))
+    _lib.check(rc, "split_kv_merge_p2p")
+
+
+def _alloc_buffer(L, nbytes):
+    import ctypes
+    from unifiedkv_b200 import _lib
+    p = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(64)
+    _lib.check(L.bpkv_peer_buffer_alloc(nbytes, ctypes.byref(p), h), "peer_exchange_alloc")
+    return p.value
+
+
+def test_p2p_merge_single_rank_calls_in_sequence(cuda):
+    """world = 1: the exchange degenerates to this rank's own slot; the output is the
+    partial itself, over several calls (the call number and parity advance on the device)."""
+    from unifiedkv_b200 import _lib
+    L = _lib.lib()
+    rows, d = 32, 128
+    buf = _alloc_buffer(L, L.bpkv_peer_exchange_bytes(1, rows, d))
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    try:
+        for it in range(5):
+            part = torch.randn(rows, d, device=cuda).to(torch.bfloat16)
+            lse = torch.randn(rows, device=cuda)
+            out = torch.empty_like(part)
+            lse_out = torch.empty(rows, device=cuda)
+            _p2p_call(L, part, lse, [buf], 0, 1, out, lse_out, status, 1 << 20)
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0
+            assert torch.equal(out, part)
+            assert torch.allclose(lse_out, lse, rtol=0, atol=1e-6)
+    finally:
+        L.bpkv_peer_buffer_free(buf)
+
+
+def test_p2p_merge_wait_runs_out_without_fault(cuda):
+    """A peer whose partial never arrives: the merge's wait gives up after max_polls,
+    reports status 1 and writes NaN rows; the GPU context stays usable.  (The second
+    'rank' is a second local buffer that nobody signals: no GPU fault is provoked.)"""
+    from unifiedkv_b200 import _lib
+    L = _lib.lib()
+    rows, d = 8, 64
+    nbytes = L.bpkv_peer_exchange_bytes(2, rows, d)
+    own, fake_peer = _alloc_buffer(L, nbytes), _alloc_buffer(L, nbytes)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    try:
+        part = torch.randn(rows, d, device=cuda)
+        lse = torch.zeros(rows, device=cuda)
+        out = torch.zeros_like(part)
+        _p2p_call(L, part, lse, [own, fake_peer], 0, 2, out, None, status, 2000)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 1
+        assert torch.isnan(out).all()
+        assert torch.equal(part + 1, part + 1)  # the context still runs kernels
+    finally:
+        L.bpkv_peer_buffer_free(own)
+        L.bpkv_peer_buffer_free(fake_peer)
+
+
+def _p2p_worker(rank, world, port, q_out):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        from unifiedkv_b200.multi_gpu import PeerMerge, local_range_lens, split_kv_decode, split_pages
+        from unifiedkv_b200.page16_native import page16_decode_attention
+        L = 20000
+        q, kc, vc, n_pages = _case(dev, L)
+        s, e = split_pages(n_pages, world)[rank]
+        bt = torch.arange(e - s, dtype=torch.int32, device=dev)[None]
+        lens = torch.tensor([local_range_lens(L, s, e)], dtype=torch.int32, device=dev)
+        peer = PeerMerge(rows=32, head_dim=128)
+        errs = []
+        g = torch.Generator(device=dev).manual_seed(11)
+        for it in range(4):  # several calls: both parities, call number advancing on the device
+            qi = (torch.randn(1, 32, 128, generator=g, device=dev) * 0.5).to(torch.bfloat16)
+            out_p2p = split_kv_decode(qi, kc[s:e], vc[s:e], bt, lens, 128 ** -0.5, 4, peer=peer)
+            out_nccl = split_kv_decode(qi, kc[s:e], vc[s:e], bt, lens, 128 ** -0.5, 4)
+            full = page16_decode_attention(qi, kc, vc, torch.arange(n_pages, dtype=torch.int32, device=dev)[None],
+                                           torch.tensor([L], dtype=torch.int32, device=dev),
+                                           softmax_scale=128 ** -0.5, n_rep=4)
+            peer.check()
+            errs.append(float(((out_p2p.float() - full.float()).abs() - 2 ** -8 * full.float().abs()).max().item()))
+            errs.append(float((out_p2p.float() - out_nccl.float()).abs().max().item()))
+        peer.close()
+        q_out.put((rank, max(errs)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_split_kv_p2p_two_ranks(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    qq = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_p2p_worker, args=(r, 2, port, qq)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(qq.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert all(err < 2e-3 for _, err in res), res

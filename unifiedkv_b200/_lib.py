@@ -23,6 +23,7 @@ BPKV_F32, BPKV_F16, BPKV_BF16 = 0, 1, 2
 _DTYPE_CODE = {torch.float32: BPKV_F32, torch.float16: BPKV_F16, torch.bfloat16: BPKV_BF16}
 
 _c_int, _c_i64, _c_sz, _c_f, _c_p = ctypes.c_int, ctypes.c_int64, ctypes.c_size_t, ctypes.c_float, ctypes.c_void_p
+_c_u32 = ctypes.c_uint32
 
 # name -> (restype, argtypes); must match include/bpkv.h
 SIGNATURES = {
@@ -42,6 +43,13 @@ SIGNATURES = {
                                             _c_int, _c_int, _c_int, _c_int, _c_int,
                                             _c_i64, _c_i64, _c_i64, _c_i64, _c_f, _c_int, _c_p]),
     "bpkv_lse_combine": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_p]),
+    "bpkv_peer_exchange_bytes": (_c_sz, [_c_int, _c_int, _c_int]),
+    "bpkv_peer_buffer_alloc": (_c_int, [_c_sz, ctypes.POINTER(_c_p), _c_p]),
+    "bpkv_peer_buffer_open": (_c_int, [_c_p, ctypes.POINTER(_c_p)]),
+    "bpkv_peer_buffer_close": (_c_int, [_c_p]),
+    "bpkv_peer_buffer_free": (_c_int, [_c_p]),
+    "bpkv_split_kv_merge_p2p": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_u32, _c_p, _c_p,
+                                         _c_p, _c_int, _c_p]),
     "bpkv_decode_append": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int,
                                     _c_i64, _c_i64, _c_i64, _c_int, _c_p]),
     "bpkv_block_score_workspace_size": (_c_sz, [_c_int, _c_int, _c_int, _c_int, _c_int]),

@@ -11,20 +11,26 @@ B200 design: one process per GPU (``torch.distributed``, NCCL over NVLink).
     requests.  No collective on the data path.
   * One very long sequence: ``split_pages`` gives each rank a contiguous range
     of the sequence's pages; each rank runs Page16 decode on its range with
-    ``lse_out`` and the ranks exchange [rows, d] fp32 partials plus [rows] lse
-    with one NCCL all-gather, merged by the log-sum-exp combine kernel.
+    ``lse_out``, and the ranks exchange the [rows, d] partials plus [rows] lse
+    and merge them by log-sum-exp.  ``PeerMerge`` does the exchange over NVLink
+    peer memory (each rank stores its partial straight into every other rank's
+    buffer, raises a flag there, and a merge kernel waits for all flags: two
+    small kernels, no collective); without it one NCCL all-gather of packed
+    partials feeds the merge kernel.
 The constructor arguments and the watermark / release methods of the
 reference coordinator are kept; KV-head sharding is not (Page16 needs all
 heads of a page on one GPU).
 """
 from __future__ import annotations
 
+import ctypes
 import heapq
 from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .pool import PagedKVPool
 
 
@@ -65,6 +71,88 @@ def exchange_partials(out_part: torch.Tensor, lse_part: torch.Tensor, group=None
     return gathered[..., :d].contiguous(), gathered[..., d].contiguous()
 
 
+class PeerMerge:
+    """NVLink peer-memory exchange + merge of split-KV partials (bpkv_split_kv_merge_p2p).
+
+    Collective set-up, on every rank of ``group`` with the same ``rows`` and
+    ``head_dim``: the library allocates this rank's exchange buffer, the CUDA IPC
+    handles travel once over the process group, and the other ranks' buffers are
+    mapped into this process.  Then ``merge`` is called on every rank in the same
+    order; the call count lives in device memory, so merges captured in a CUDA
+    graph replay correctly.  ``close`` (collective) unmaps and frees.
+    """
+
+    def __init__(self, rows: int, head_dim: int, group=None, device: Optional[torch.device] = None,
+                 max_polls: int = 1 << 24):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.rows, self.head_dim = int(rows), int(head_dim)
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        self.max_polls = int(max_polls)
+        L = _lib.lib()
+        nbytes = L.bpkv_peer_exchange_bytes(self.world, self.rows, self.head_dim)
+        if nbytes == 0:
+            raise RuntimeError(f"peer_exchange_shape:world_{self.world}_rows_{rows}_head_dim_{head_dim}")
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        with torch.cuda.device(self.device):
+            _lib.check(L.bpkv_peer_buffer_alloc(nbytes, ctypes.byref(own), handle), "peer_exchange_alloc")
+        self._own = own.value
+        handles: List[bytes] = [b""] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self._opened: List[int] = []
+        bufs = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == self.rank:
+                    bufs.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                _lib.check(L.bpkv_peer_buffer_open(h, ctypes.byref(p)), "peer_exchange_open")
+                self._opened.append(p.value)
+                bufs.append(p.value)
+        self._bufs = (ctypes.c_void_p * self.world)(*bufs)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def merge(self, part_out: torch.Tensor, part_lse: torch.Tensor, out_dtype: Optional[torch.dtype] = None,
+              lse_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """part_out [rows, d] (any of fp32/fp16/bf16, this rank's partial), part_lse fp32 [rows]
+        -> merged [rows, d] in part_out's dtype (out_dtype must match it)."""
+        rows, d = int(part_out.shape[0]), int(part_out.shape[1])
+        if rows != self.rows or d != self.head_dim or (out_dtype is not None and out_dtype != part_out.dtype):
+            raise RuntimeError("peer_exchange_shape:merge")
+        part_out = part_out.contiguous()
+        part_lse = part_lse.reshape(rows).float().contiguous()
+        out = torch.empty_like(part_out)
+        with torch.cuda.device(self.device):
+            rc = _lib.lib().bpkv_split_kv_merge_p2p(
+                part_out.data_ptr(), part_lse.data_ptr(), self._bufs, self.rank, self.world, rows, d,
+                self.max_polls, out.data_ptr(), _lib.ptr(lse_out), self.status.data_ptr(),
+                _lib.dtype_code(part_out.dtype), _lib.stream_ptr(self.device))
+        _lib.check(rc, "split_kv_merge_p2p")
+        return out
+
+    def check(self) -> None:
+        """Host check of the device status (synchronises): raises if a wait ran out."""
+        if int(self.status.item()) != 0:
+            raise RuntimeError("peer_exchange_timeout: a rank's partial did not arrive")
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no rank still stores into a buffer that is about to go
+        L = _lib.lib()
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                _lib.check(L.bpkv_peer_buffer_close(p), "peer_exchange_close")
+            self._opened = []
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            if self._own is not None:
+                _lib.check(L.bpkv_peer_buffer_free(self._own), "peer_exchange_free")
+                self._own = None
+
+
 def _native_merge(parts: torch.Tensor, lses: torch.Tensor, out_dtype: torch.dtype):
     from .page16_native import lse_combine
     return lse_combine(parts, lses, out_dtype, return_lse=True)
@@ -72,19 +160,22 @@ def _native_merge(parts: torch.Tensor, lses: torch.Tensor, out_dtype: torch.dtyp
 
 def split_kv_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, local_block_table: torch.Tensor,
                     local_lens: torch.Tensor, softmax_scale: float, n_rep: int, group=None,
-                    merge: Optional[Callable] = None) -> torch.Tensor:
+                    merge: Optional[Callable] = None, peer: Optional[PeerMerge] = None) -> torch.Tensor:
     """Decode one (or a few) sequences whose pages are split across ranks.
 
     Each rank passes q (identical on all ranks, [B, h_q, d]), its own pool
     view, the block table of ITS page range and the token count in that range.
     Returns the merged [B, h_q, d] output on every rank.  A rank whose range
-    is empty contributes lse = -inf (nothing).
+    is empty contributes lse = -inf (nothing).  With ``peer`` (a PeerMerge for
+    rows = B*h_q) the partials travel over NVLink peer memory instead of NCCL.
     """
     from .page16_native import page16_decode_attention
     B, hq, d = [int(x) for x in q.shape]
     lse = torch.empty((B, hq), dtype=torch.float32, device=q.device)
     part = page16_decode_attention(q, k_cache, v_cache, local_block_table, local_lens, softmax_scale=softmax_scale,
                                    n_rep=n_rep, lse_out=lse)
+    if peer is not None:
+        return peer.merge(part.reshape(B * hq, d), lse.reshape(B * hq)).reshape(B, hq, d)
     parts, lses = exchange_partials(part.float().reshape(B * hq, d), lse.reshape(B * hq), group)
     merge = merge or _native_merge
     out, _ = merge(parts, lses, q.dtype)

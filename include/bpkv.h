@@ -157,14 +157,14 @@ BPKV_API int bpkv_lse_combine(const float* part_out, const float* part_lse, void
  *   exchange the handles between the processes, then on every rank
  *   bpkv_peer_buffer_open(handle_of_rank_r, &bufs[r]) for r != rank (bufs[rank] = own).
  * Per call (every rank makes the same sequence of calls; the call number is
- * kept in the buffer itself, so the two kernels of a call can be captured in a
- * CUDA graph and replayed):
+ * kept in the buffer itself, so the call's kernel can be captured in a CUDA
+ * graph and replayed):
  *   bpkv_split_kv_merge_p2p: this rank's partial part_out [rows, head_dim]
  *   (dtype) with natural-log part_lse [rows] is stored into every rank's
  *   buffer over NVLink, a flag per rank marks it landed, then every rank
  *   waits for all flags of this epoch and writes the merged out [rows,
  *   head_dim] (and lse_out [rows] if not null).  A wait gives up after
- *   max_polls polls (~64 ns apart): *status is set to 1 and the rows are NaN.
+ *   max_polls polls: *status is set to 1 and the rows are NaN.
  * Teardown: bpkv_peer_buffer_close(bufs[r]) for r != rank, after a barrier
  * bpkv_peer_buffer_free(own).  world <= 8; head_dim % 4 == 0.  No multicast.
  * ------------------------------------------------------------------------ */

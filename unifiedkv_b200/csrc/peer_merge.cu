@@ -8,32 +8,33 @@
 //   uint32 flag[2][kMaxRanks]              (flag[par][r] = epoch: rank r's data landed)
 //   uint32 count[2][kMaxRanks]             (local: finished chunks per peer)
 //   uint32 epoch, merged                   (local: calls completed, merge CTAs done)
-// Call number e (kept in device memory, so the kernel pair can be captured in a
-// CUDA graph and replayed) uses parity e & 1: a peer may already write call
+// Call number e (kept in device memory, so the kernel can be captured in a CUDA
+// graph and replayed) uses parity e & 1: a peer may already write call
 // e+1 while this rank still merges e; e+2 cannot start before this rank has
 // finished e (its send of e+1 comes after).
 //
-// peer_send_kernel:   CTA (p, c) stores chunk c of this rank's partial (T out,
-//                     fp32 lse) into rank p's buffer with plain stores through
-//                     the IPC mapping (NVLink), fences at system scope, and the
-//                     last chunk to finish raises flag[par][rank] = e in rank
-//                     p's buffer with a release store.
-// peer_merge_kernel:  waits (bounded) until every rank's flag for this epoch
-//                     is up in the own buffer, then merges the world partials
-//                     per row: M = max lse, W = sum exp(lse - M), out = sum
-//                     exp(lse - M) o / W, lse_out = M + log W.
-// The two kernels are separate launches so that no CTA waits on another CTA of
-// its own grid: the merge waits only on sends that already ran (its own rank's,
-// earlier in the stream) or run on other GPUs.  A wait that runs out sets
-// *status = 1 and writes NaN rows; the context stays usable.  No multicast, no
-// TMA: plain loads and stores.
+// peer_exchange_kernel<T>, one launch per call:
+//   1. CTA u = (peer index i, chunk c) stores chunk c of this rank's partial
+//      (T out, fp32 lse) into peer (rank + 1 + i) % world's buffer with plain
+//      stores through the IPC mapping (NVLink), fences at system scope, and
+//      the last chunk for that peer raises flag[par][rank] = e there with a
+//      release store.  The rank's own partial is not copied: the merge reads
+//      it in place.
+//   2. every CTA waits (bounded spin on acquire loads) until the flags of all
+//      other ranks for call e are up in the own buffer.  Those flags are set
+//      by the kernels of the other GPUs only, never by a CTA of this grid.
+//   3. the CTAs merge rows r = blockIdx.x*8 + warp, stride gridDim.x*8: M =
+//      max lse, W = sum exp(lse - M), out = sum exp(lse - M) o / W, lse_out =
+//      M + log W; the last CTA to finish advances the call number.
+// A wait that runs out sets *status = 1 and writes NaN rows; the context stays
+// usable.  No multicast, no TMA: plain loads and stores.
 #include "common.cuh"
 
 namespace bpkv {
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr int kSendThreads = 256, kMergeWarps = 8;
+constexpr int kSendThreads = 256;
 
 struct PeerArgs {
   float* bufs[kMaxRanks];  // every rank's exchange buffer as mapped in this process (own included)
@@ -69,39 +70,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kSendThreads) peer_send_kernel(const __grid_constant__ PeerArgs a) {
-  const int p = blockIdx.x, c = blockIdx.y;
-  const uint32_t epoch = *epoch_ptr(a.bufs[a.rank], a) + 1u;  // this call's number
-  const int par = static_cast<int>(epoch & 1u);
-  float* dst = a.bufs[p] + ((static_cast<int64_t>(par) * a.world + a.rank) * a.rows) * row_floats(a.D);
-  const T* src = reinterpret_cast<const T*>(a.part_out);
-  const int r0 = c * a.rows_per_chunk, r1 = min(a.rows, r0 + a.rows_per_chunk);
-  const int q4 = a.D / 4;  // float4 per row (D % 4 == 0)
-  for (int e = threadIdx.x; e < (r1 - r0) * (q4 + 1); e += blockDim.x) {
-    const int r = r0 + e / (q4 + 1), j = e % (q4 + 1);
-    float* drow = dst + static_cast<int64_t>(r) * row_floats(a.D);
-    if (j < q4) {
-      const T* s = src + static_cast<int64_t>(r) * a.D + 4 * j;
-      *reinterpret_cast<float4*>(drow + 4 * j) =
-          make_float4(Elem<T>::to_f(s[0]), Elem<T>::to_f(s[1]), Elem<T>::to_f(s[2]), Elem<T>::to_f(s[3]));
-    } else {
-      drow[a.D] = a.part_lse[r];
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();  // this chunk's stores before the count below
-    uint32_t* cnt = count_ptr(a.bufs[a.rank], a, par, p);
-    if (atomicAdd(cnt, 1u) == static_cast<uint32_t>(a.chunks - 1)) {
-      *cnt = 0u;               // ready for epoch + 2 (same parity)
-      __threadfence_system();  // every chunk's stores (seen through the count) before the flag
-      st_release_sys(flag_ptr(a.bufs[p], a, par, a.rank), epoch);
-    }
-  }
-}
-
-// One merged row, one warp: M = max lse, out = sum exp(lse - M) o / sum exp(lse - M).
+// One merged row, one warp.  Rank q's partial comes from the own buffer, the
+// own rank's from part_out / part_lse in place.
 template <typename T>
 __device__ void merge_row(const PeerArgs& a, const float* own, int par, int r, bool failed, int lane) {
   T* out = reinterpret_cast<T*>(a.out) + static_cast<int64_t>(r) * a.D;
@@ -113,8 +83,14 @@ __device__ void merge_row(const PeerArgs& a, const float* own, int par, int r, b
   }
   const float* base = own + (static_cast<int64_t>(par) * a.world * a.rows + r) * row_floats(a.D);
   const int64_t slot = static_cast<int64_t>(a.rows) * row_floats(a.D);
+  const T* mine = reinterpret_cast<const T*>(a.part_out) + static_cast<int64_t>(r) * a.D;
+  float lse[kMaxRanks];
   float M = -INFINITY;
-  for (int q = 0; q < a.world; ++q) M = fmaxf(M, base[q * slot + a.D]);
+#pragma unroll
+  for (int q = 0; q < kMaxRanks; ++q) {
+    lse[q] = q >= a.world ? -INFINITY : (q == a.rank ? a.part_lse[r] : base[q * slot + a.D]);
+    M = fmaxf(M, lse[q]);
+  }
   if (M == -INFINITY) {  // no rank had keys for this row (the reference's 0/0)
     for (int d = lane; d < a.D; d += 32) out[d] = Elem<T>::from_f(nan);
     if (a.lse_out != nullptr && lane == 0) a.lse_out[r] = -INFINITY;
@@ -124,29 +100,64 @@ __device__ void merge_row(const PeerArgs& a, const float* own, int par, int r, b
   float W = 0.f;
 #pragma unroll
   for (int q = 0; q < kMaxRanks; ++q) {
-    w[q] = q < a.world ? expf(base[q * slot + a.D] - M) : 0.f;
+    w[q] = q < a.world ? expf(lse[q] - M) : 0.f;
     W += w[q];
   }
   const float invW = 1.f / W;
   for (int d = lane; d < a.D; d += 32) {
     float acc = 0.f;
 #pragma unroll
-    for (int q = 0; q < kMaxRanks; ++q)
-      if (q < a.world && w[q] > 0.f) acc += w[q] * base[q * slot + d];
+    for (int q = 0; q < kMaxRanks; ++q) {
+      if (q >= a.world || !(w[q] > 0.f)) continue;
+      acc += w[q] * (q == a.rank ? Elem<T>::to_f(mine[d]) : base[q * slot + d]);
+    }
     out[d] = Elem<T>::from_f(acc * invW);
   }
   if (a.lse_out != nullptr && lane == 0) a.lse_out[r] = M + logf(W);
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kMergeWarps * 32) peer_merge_kernel(const __grid_constant__ PeerArgs a) {
+__global__ void __launch_bounds__(kSendThreads) peer_exchange_kernel(const __grid_constant__ PeerArgs a) {
   __shared__ int s_failed;
   float* own = a.bufs[a.rank];
-  const uint32_t epoch = *epoch_ptr(own, a) + 1u;  // stored back by the last CTA below
+  const uint32_t epoch = *epoch_ptr(own, a) + 1u;  // this call; stored back by the last CTA below
   const int par = static_cast<int>(epoch & 1u);
+  const int n_send = (a.world - 1) * a.chunks;
+  // ---- 1. send ----
+  if (static_cast<int>(blockIdx.x) < n_send) {
+    const int i = blockIdx.x / a.chunks, c = blockIdx.x % a.chunks;
+    const int p = (a.rank + 1 + i) % a.world;
+    float* dst = a.bufs[p] + ((static_cast<int64_t>(par) * a.world + a.rank) * a.rows) * row_floats(a.D);
+    const T* src = reinterpret_cast<const T*>(a.part_out);
+    const int r0 = c * a.rows_per_chunk, r1 = min(a.rows, r0 + a.rows_per_chunk);
+    const int q4 = a.D / 4;  // float4 per row (D % 4 == 0)
+    for (int e = threadIdx.x; e < (r1 - r0) * (q4 + 1); e += blockDim.x) {
+      const int r = r0 + e / (q4 + 1), j = e % (q4 + 1);
+      float* drow = dst + static_cast<int64_t>(r) * row_floats(a.D);
+      if (j < q4) {
+        const T* sp = src + static_cast<int64_t>(r) * a.D + 4 * j;
+        *reinterpret_cast<float4*>(drow + 4 * j) =
+            make_float4(Elem<T>::to_f(sp[0]), Elem<T>::to_f(sp[1]), Elem<T>::to_f(sp[2]), Elem<T>::to_f(sp[3]));
+      } else {
+        drow[a.D] = a.part_lse[r];
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();  // this chunk's stores before the count below
+      uint32_t* cnt = count_ptr(own, a, par, p);
+      if (atomicAdd(cnt, 1u) == static_cast<uint32_t>(a.chunks - 1)) {
+        *cnt = 0u;               // ready for call e + 2 (same parity)
+        __threadfence_system();  // every chunk's stores (seen through the count) before the flag
+        st_release_sys(flag_ptr(a.bufs[p], a, par, a.rank), epoch);
+      }
+    }
+  }
+  // ---- 2. wait for the other ranks' partials of this call ----
   if (threadIdx.x == 0) {
     int failed = 0;
     for (int q = 0; q < a.world && !failed; ++q) {
+      if (q == a.rank) continue;
       const uint32_t* f = flag_ptr(own, a, par, q);
       uint32_t polls = 0;
       while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
@@ -154,17 +165,17 @@ __global__ void __launch_bounds__(kMergeWarps * 32) peer_merge_kernel(const __gr
           failed = 1;
           break;
         }
-        __nanosleep(64);
       }
     }
     s_failed = failed;
     if (failed) atomicExch(a.status, 1);
   }
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * kMergeWarps + warp;
-  if (r < a.rows) merge_row<T>(a, own, par, r, s_failed != 0, lane);
-  // the last CTA to finish advances the call number for the next call
+  // ---- 3. merge ----
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  for (int r = blockIdx.x * nw + warp; r < a.rows; r += gridDim.x * nw) merge_row<T>(a, own, par, r, s_failed != 0, lane);
+  // the last CTA to finish advances the call number for the next call (every
+  // CTA has read it by the time it counts itself done)
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -262,17 +273,13 @@ extern "C" BPKV_API int bpkv_split_kv_merge_p2p(const void* part_out, const floa
   a.world = world;
   a.rows = rows;
   a.D = head_dim;
-  a.rows_per_chunk = max(1, (16384 / 4) / (head_dim + 4));  // about 16 KB of rows per chunk
+  // about 8 chunks per peer (parallel stores), at most ~16 KB of rows each
+  a.rows_per_chunk = max(1, min((16384 / 4) / (head_dim + 4), (rows + 7) / 8));
   a.chunks = (rows + a.rows_per_chunk - 1) / a.rows_per_chunk;
   a.max_polls = max_polls;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const dim3 sgrid(world, a.chunks);
-  const int mgrid = (rows + kMergeWarps - 1) / kMergeWarps;
-#define BPKV_P2P(TY)                                                    \
-  do {                                                                  \
-    peer_send_kernel<TY><<<sgrid, kSendThreads, 0, st>>>(a);           \
-    peer_merge_kernel<TY><<<mgrid, kMergeWarps * 32, 0, st>>>(a);      \
-  } while (0)
+  const int grid = max((world - 1) * a.chunks, 1);
+#define BPKV_P2P(TY) peer_exchange_kernel<TY><<<grid, kSendThreads, 0, st>>>(a)
   if (dtype == BPKV_BF16) BPKV_P2P(__nv_bfloat16);
   else if (dtype == BPKV_F16) BPKV_P2P(__half);
   else BPKV_P2P(float);

@@ -13,9 +13,9 @@ B200 design: one process per GPU (``torch.distributed``, NCCL over NVLink).
     of the sequence's pages; each rank runs Page16 decode on its range with
     ``lse_out``, and the ranks exchange the [rows, d] partials plus [rows] lse
     and merge them by log-sum-exp.  ``PeerMerge`` does the exchange over NVLink
-    peer memory (each rank stores its partial straight into every other rank's
-    buffer, raises a flag there, and a merge kernel waits for all flags: two
-    small kernels, no collective); without it one NCCL all-gather of packed
+    peer memory in one kernel (each rank stores its partial straight into every
+    other rank's buffer and raises a flag there, then waits for the other ranks'
+    flags and merges; no collective); without it one NCCL all-gather of packed
     partials feeds the merge kernel.
 The constructor arguments and the watermark / release methods of the
 reference coordinator are kept; KV-head sharding is not (Page16 needs all
@@ -83,7 +83,7 @@ class PeerMerge:
     """
 
     def __init__(self, rows: int, head_dim: int, group=None, device: Optional[torch.device] = None,
-                 max_polls: int = 1 << 24):
+                 max_polls: int = 1 << 22):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)

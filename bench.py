@@ -58,7 +58,7 @@ def algorithmic_bytes(lens) -> int:
     """Bytes one layer's decode must move: KV of every token, q, out, table, lens."""
     kv = int(np.sum(lens)) * KV_BYTES_PER_TOKEN
     pages = int(np.sum((lens + 15) // 16))
-    return kv + 2 * BATCH * HQ * D * 2 + 4 * pages + 4 * BATCH
+    return kv + 2 * len(lens) * HQ * D * 2 + 4 * pages + 4 * len(lens)
 
 
 class ClockSampler:
@@ -196,10 +196,22 @@ def run_reference(args, rank: int, world: int) -> None:
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
-def setup_rank(rank: int, device, seed_base: int = 2024, small: bool = False):
+def setup_rank(rank: int, device, seed_base: int = 2024, small: bool = False, world: int = 1):
+    """This rank's share of the workload.  One GPU: 32 requests.  N GPUs: the global batch of
+    32*N requests is drawn once (same seed on every rank) and assigned by the library's
+    request sharding (unifiedkv_b200.multi_gpu.shard_requests, longest-first over page
+    counts), so every rank holds about the same KV bytes."""
     import torch
     global LAYERS
-    rng, lens = make_requests(seed_base + rank)
+    if world > 1:
+        from unifiedkv_b200.multi_gpu import shard_requests
+        all_lens = np.random.default_rng(seed_base).integers(CTX_LO, CTX_HI + 1, size=BATCH * world).astype(np.int32)
+        owner = np.asarray(shard_requests(all_lens.tolist(), world))
+        lens = all_lens[owner == rank]
+        rng = np.random.default_rng(seed_base + 1000 + rank)
+    else:
+        rng, lens = make_requests(seed_base + rank)
+    nreq = len(lens)
     need = (lens + 15) // 16
     if small:  # profiling case: one layer, pool of just the needed pages (~2.5 GB)
         LAYERS = 1
@@ -216,12 +228,12 @@ def setup_rank(rank: int, device, seed_base: int = 2024, small: bool = False):
         k_pool[l].normal_(0.0, 0.5, generator=g)
         v_pool[l].normal_(0.0, 0.5, generator=g)
     perm = rng.permutation(n_pages).astype(np.int32)
-    bt = np.zeros((BATCH, int(need.max())), np.int32)
+    bt = np.zeros((nreq, int(need.max())), np.int32)
     off = 0
     for b, n in enumerate(need):  # all layers share block ids (core/scheduler.py:1141)
         bt[b, :n] = perm[off:off + n]
         off += int(n)
-    qs = [(torch.randn((BATCH, HQ, D), generator=g, device=device) * 0.5).to(torch.bfloat16) for _ in range(LAYERS)]
+    qs = [(torch.randn((nreq, HQ, D), generator=g, device=device) * 0.5).to(torch.bfloat16) for _ in range(LAYERS)]
     return dict(k_pool=k_pool, v_pool=v_pool, bt=bt, lens=lens, qs=qs, n_pages=n_pages)
 
 
@@ -232,7 +244,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    st = setup_rank(rank, device, small=args.profile_small)
+    st = setup_rank(rank, device, small=args.profile_small, world=world)
     k_pool, v_pool, qs = st["k_pool"], st["v_pool"], st["qs"]
     bt_d = torch.from_numpy(st["bt"]).to(device)
     lens_d = torch.from_numpy(st["lens"]).to(device)
@@ -340,7 +352,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.5) q/k/v, random block tables)",
         "config": {"workload": WORKLOAD, "layers": LAYERS, "batch_per_gpu": BATCH, "global_batch": BATCH * world,
                    "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "pool_pages_per_gpu": st["n_pages"],
-                   "mean_ctx_rank0": float(np.mean(st["lens"])), "parallelism": f"request-sharded x{world}",
+                   "mean_ctx_rank0": float(np.mean(st["lens"])),
+                   "parallelism": f"request-sharded x{world}" + ("" if world == 1 else
+                                  " (global batch drawn once, longest-first page balancing)"),
                    "l2": "no flush: each launch reads ~2.4 GB of KV, far above the 126 MB L2"},
         "tokens_per_s": round(tokens_per_s, 2),
         "hbm_frac_of_measured": round(gbs / world / peak, 4),

@@ -508,8 +508,7 @@ int launch_score(ScoreParams& p, float* out, int N, int smooth, int per_head, cu
     int rc = score_tc_pass(t, D, dt, 1, st);
     if (rc != BPKV_ERR_UNSUPPORTED) {
       if (rc != BPKV_OK) return rc;
-      const int nrows = p.Hq * p.Wp;
-      stats_reduce_kernel<<<(nrows * 32 + 255) / 256, 256, 0, st>>>(p.ml_part, p.ml, nrows, t.n_chunks);
+      // (pass 2 merges the per-range row statistics itself: no stats_reduce launch)
       rc = score_tc_pass(t, D, dt, 2, st);
       if (rc != BPKV_OK) return rc;
       block_reduce_kernel<<<rgrid, 256, 0, st>>>(p.headmax, out, p.Hkv, t.hm_slots, p.Tm, N, smooth, per_head);

@@ -146,9 +146,19 @@ __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_cons
   load_q<T>(p, qs, g, PASS == 1 ? mtiles * 128 : rows, kThreads);
   cp_async_commit();
   if constexpr (PASS == 2) {
+    // merge pass 1's partial (m, l) of this group's window rows over the token ranges
+    // (fixed order) -> -(m + log2 l) per row, -inf for padding rows
     for (int r = tid; r < rows; r += kThreads) {
-      const float2 st = p.ml[static_cast<int64_t>(g) * p.n_rep * p.Wp + r];
-      s_off[r] = (r % p.Wp) < p.W ? -(st.x + log2f(st.y)) : -INFINITY;
+      if ((r % p.Wp) >= p.W) {
+        s_off[r] = -INFINITY;
+        continue;
+      }
+      const float2* src = p.ml_part + (static_cast<int64_t>(g) * rows + r) * p.n_chunks;
+      float m = -INFINITY;
+      for (int c = 0; c < p.n_chunks; ++c) m = fmaxf(m, src[c].x);
+      float l = 0.f;
+      for (int c = 0; c < p.n_chunks; ++c) l += src[c].y * exp2f(src[c].x - m);
+      s_off[r] = -(m + log2f(l));
     }
   }
   cp_async_wait<0>();

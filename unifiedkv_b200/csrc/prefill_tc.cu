@@ -91,6 +91,7 @@ constexpr int kSoftmaxWarps = kGroups * kGroupWarps;  // warps 0..15
 constexpr int kLoadWarp = kSoftmaxWarps;       // warp 16: TMA / cp.async loads
 constexpr int kMmaWarp = kSoftmaxWarps + 1;    // warp 17: tcgen05.mma issue
 constexpr int kThreads = (kSoftmaxWarps + 2) * 32;
+static_assert(kThreads == (kMmaWarp + 1) * 32, "the MMA-issue warp is the last warp");
 constexpr int kMaxPagesSmem = 2048;            // block-table entries staged in shared memory
 constexpr int kSmemBytes = kGroups * kQBytes + (kNK + kNV) * kKVBytes + 1024 /*align*/ + 256 + 4 * kMaxPagesSmem +
                             4 * kGroups * 2 * kSplit * kBM /*row-max exchange*/ + 4 * kGroups * kSplit * kBM /*row sums*/;

@@ -507,7 +507,7 @@ def run_compress(args):
                    "selection": "per_kv_head" if per_head else "shared across kv heads (reference)"},
         "algorithmic_gbs": round(gbs, 1), "hbm_frac_of_measured": round(gbs / hbm, 4),
         "tflops": round(flops_layer * layers / (ms * 1e-3) / 1e12, 2),
-        "gpu_launches": 6 * layers * args.steps,
+        "gpu_launches": 5 * layers * args.steps,  # score pass 1, pass 2, block reduce, top-k, compaction
     }), flush=True)
 
 

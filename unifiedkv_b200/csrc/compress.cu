@@ -428,6 +428,38 @@ __global__ void page_compact_kernel(const uint8_t* k_src, const uint8_t* v_src, 
   uint8_t* dst = (is_v ? v_pool : k_pool) + static_cast<int64_t>(dst_pages[j]) * page_stride_b;
   const int vec_per_row = row_bytes / static_cast<int>(sizeof(V));
   const int total = kPage * Hkv * vec_per_row;
+  if (vec_per_row <= static_cast<int>(blockDim.x) && blockDim.x % vec_per_row == 0) {
+    // Each thread keeps one column vi of the rows (slot, head) it visits; the source token
+    // is computed once per row, and the loads of a batch of rows go out before its stores.
+    constexpr int kBatch = 8;
+    const int vi = threadIdx.x % vec_per_row;
+    const int rstep = blockDim.x / vec_per_row;
+    const int nrows = kPage * Hkv;
+    for (int r0 = threadIdx.x / vec_per_row; r0 < nrows; r0 += rstep * kBatch) {
+      V val[kBatch];
+      int64_t doff[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int rh = r0 + u * rstep;
+        doff[u] = -1;
+        if (rh >= nrows) continue;
+        const int h = rh % Hkv, slot = rh / Hkv;
+        const int p = j * kPage + slot;
+        if (p >= eff_len) continue;  // slots past the compacted length stay untouched
+        const int64_t t = compact_src_token(p, L, sink, obs, kb, selected + h * sel_stride_h);
+        if (t >= 0) {
+          val[u] = __ldg(reinterpret_cast<const V*>(src + h * src_sh_b + t * src_st_b) + vi);
+        } else {
+          memset(&val[u], 0, sizeof(V));
+        }
+        doff[u] = slot * dst_st_b + h * dst_sh_b + static_cast<int64_t>(vi) * sizeof(V);
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        if (doff[u] >= 0) *reinterpret_cast<V*>(dst + doff[u]) = val[u];
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
     const int vi = i % vec_per_row;
     const int rh = i / vec_per_row;

@@ -174,3 +174,21 @@ def test_selection_engine_transaction(cuda, monkeypatch):
     with pytest.raises(torch.cuda.OutOfMemoryError):
         eng._selected_writeback_transaction(8, raw, selected, eff, L, "ratio")
     assert pool.n_free == free_before and eng.writeback_transaction_rollbacks == 1
+
+
+def test_block_scores_large_logits(cuda):
+    """Window queries 40x larger than usual: per-row maxima jump by far more than 2^8
+    between K tiles, exercising the statistics pass's rescale and its recompute for
+    jumps above 2^120; scores still match the fp64 oracle."""
+    from unifiedkv_b200.compress import SMOOTH_ALWAYS, block_scores
+    K, V, Q, _ = compress_case(seed=71, h_kv=8, L=6000, d=128, n_rep=4, window=64)
+    ramp = np.linspace(0.1, 4.0, 6000, dtype=np.float32)[None, :, None]
+    tk = _t(K * ramp, cuda, torch.bfloat16)
+    tq = _t(Q * 40.0, cuda, torch.bfloat16)
+    s = block_scores(tk, tq, 64, 64, smooth=SMOOTH_ALWAYS)
+    torch.cuda.synchronize()
+    ref = oc.block_scores(tk.float().cpu().numpy(), tq.float().cpu().numpy(), 64, 64)
+    got = s.cpu().numpy()
+    assert np.isfinite(got).all()
+    # most blocks carry (close to) zero mass here: compare relative to the largest score
+    assert np.max(np.abs(got - ref)) < 1e-4 * np.max(ref) + 1e-7, np.max(np.abs(got - ref))

@@ -224,3 +224,17 @@ def test_shape_errors_use_reference_tokens(cuda):
         page16_decode_attention(q, kc[:, :8], kc[:, :8], bt, lens, softmax_scale=0.1, n_rep=1)
     with pytest.raises(RuntimeError, match="page16_native_shape_unsupported:block_table_batch"):
         page16_decode_attention(q[:, :4], kc, kc, bt[:1], lens, softmax_scale=0.1, n_rep=1)
+
+
+def test_decode_large_logits(cuda):
+    """Logits of several hundred (natural log units) with keys growing along the
+    sequence: the running max keeps moving and exp underflows for most keys."""
+    q, k, v, bt, lens = page16_case(seed=61, batch=3, hq=32, hkv=8, d=128, lens=(5000, 37, 900), num_pages=400,
+                                    scale_std=1.0)
+    ramp = np.linspace(0.2, 6.0, 16 * 400, dtype=np.float32).reshape(400, 16, 1, 1)
+    k = (k * ramp).astype(np.float32)
+    q = (q * 8.0).astype(np.float32)
+    out, _, (qr, kr, vr) = _run(cuda, q, k, v, bt, lens, torch.bfloat16)
+    ref = page16_decode_reference(qr, kr, vr, bt, lens, 1 / math.sqrt(128), 4)
+    assert np.isfinite(out).all()
+    assert _err(out, ref, torch.bfloat16) < 2e-3

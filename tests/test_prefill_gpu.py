@@ -190,3 +190,21 @@ def test_paged_chunk_prefill_past_beyond_staged_table(cuda):
     assert need[0] > 2048
     out = paged_chunk_prefill(q, kc, vc, torch.from_numpy(bt).to(cuda), past, chunk, d ** -0.5, hq // hkv)
     _check_paged(cuda, out, kc, vc, bt, q, totals, need, chunk, hkv, d, dtype)
+
+
+def test_paged_prefill_large_logits(cuda):
+    """Scores spanning hundreds of log2 units: the lazily moved reference max is raised
+    many times (rescaling O in TMEM), and masked rows mix with rows of huge logits."""
+    from unifiedkv_b200.chunked_prefill import paged_chunk_prefill
+    hq, hkv, d, dtype = 32, 8, 128, torch.bfloat16
+    past, chunk = [900, 0, 3000], [200, 130, 64]
+    kc, vc, bt, q, totals, need = _paged_case(cuda, hq, hkv, d, dtype, past, chunk, seed=91)
+    # keys grow along the sequence, so later tiles keep raising each row's max
+    for b in range(len(past)):
+        pages = torch.from_numpy(bt[b, :need[b]].astype(np.int64)).to(cuda)
+        ramp = torch.linspace(0.2, 6.0, need[b] * 16, device=cuda).reshape(need[b], 16, 1, 1)
+        kc[pages] = (kc[pages].float() * ramp).to(dtype)
+    q = (q.float() * 8.0).to(dtype)
+    out = paged_chunk_prefill(q, kc, vc, torch.from_numpy(bt).to(cuda), past, chunk, d ** -0.5, hq // hkv)
+    assert torch.isfinite(out.float()).all()
+    _check_paged(cuda, out, kc, vc, bt, q, totals, need, chunk, hkv, d, dtype)

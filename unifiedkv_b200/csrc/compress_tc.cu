@@ -267,8 +267,11 @@ __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_cons
             up2(acc, sa, sb);
             return sa + sb;
           };
-          float mx;
-          if (m_ref == -INFINITY) {  // no reference yet: take this tile's max first
+          // tcgen05.ld is warp-collective: every TMEM load below is executed by the whole
+          // warp (branches on __any_sync), each lane keeping or dropping the result by its
+          // own row's condition
+          const bool no_ref = m_ref == -INFINITY;
+          if (__any_sync(0xffffffffu, no_ref)) {  // no reference yet: take this tile's max first
             float m4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
             for (int c0 = 0; c0 < 64; c0 += 32) {
@@ -277,23 +280,27 @@ __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_cons
 #pragma unroll
               for (int c = 0; c < 32; ++c) m4[c & 3] = fmaxf(m4[c & 3], a[c]);
             }
-            m_ref = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;  // scale > 0
+            if (no_ref) m_ref = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * p.scale_log2;  // scale > 0
           }
-          if (m_ref != -INFINITY) {
-            // one pass with the current (lazily moved) reference; the tile's max comes out of it
-            float sum = tile_sum(m_ref, mx);
-            const float mxs = mx * p.scale_log2;
-            if (mxs > m_ref + 8.f) {
-              if (mxs > m_ref + 120.f) {
-                sum = tile_sum(mxs, mx);  // terms may have overflowed: redo with the new reference
-              } else {
-                sum *= fast_exp2(m_ref - mxs);
-              }
-              l = l * fast_exp2(m_ref - mxs) + sum;
-              m_ref = mxs;
-            } else {
-              l += sum;
-            }
+          // one pass with the current (lazily moved) reference; the tile's max comes out of it.
+          // A row still without a reference has only -inf scores: its terms are 0 for any ref.
+          const bool has_ref = m_ref != -INFINITY;
+          float mx;
+          float sum = tile_sum(has_ref ? m_ref : 0.f, mx);
+          const float mxs = mx * p.scale_log2;
+          const bool moved = has_ref && mxs > m_ref + 8.f;
+          const bool redo = moved && mxs > m_ref + 120.f;  // terms may have overflowed
+          if (__any_sync(0xffffffffu, redo)) {
+            float mx2;
+            const float sum2 = tile_sum(redo ? mxs : (has_ref ? m_ref : 0.f), mx2);
+            if (redo) sum = sum2;
+          }
+          if (moved) {
+            if (!redo) sum *= fast_exp2(m_ref - mxs);
+            l = l * fast_exp2(m_ref - mxs) + sum;
+            m_ref = mxs;
+          } else if (has_ref) {
+            l += sum;
           }
         }
         release(j);

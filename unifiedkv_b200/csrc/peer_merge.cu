@@ -160,8 +160,12 @@ __global__ void __launch_bounds__(kSendThreads) peer_exchange_kernel(const __gri
       if (q == a.rank) continue;
       const uint32_t* f = flag_ptr(own, a, par, q);
       uint32_t polls = 0;
+      uint64_t t0;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
       while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
-        if (++polls > a.max_polls) {
+        uint64_t t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        if (++polls > a.max_polls || t - t0 > 4000000000ull) {  // poll count or 4 s, whichever first
           failed = 1;
           break;
         }

@@ -17,10 +17,20 @@ __device__ __forceinline__ void mbar_init(uint32_t addr, uint32_t count) {
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
 }
-// Waits for the phase with parity `parity` to complete.  Gives up after
-// `max_iters` polls and returns false (the caller records an error and
-// abandons the tile rather than hanging the GPU).
-__device__ __forceinline__ bool mbar_wait(uint32_t addr, uint32_t parity, uint32_t max_iters = (1u << 24)) {
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits for the phase with parity `parity` to complete.  Gives up and returns
+// false (the caller records an error and abandons the tile rather than hanging
+// the GPU) after `max_iters` polls or `max_ns` nanoseconds, whichever comes
+// first: a try_wait may itself suspend the thread for a hardware-chosen time,
+// so the poll count alone does not bound the wait in time.
+__device__ __forceinline__ bool mbar_wait(uint32_t addr, uint32_t parity, uint32_t max_iters = (1u << 24),
+                                          uint64_t max_ns = 2000000000ull) {
+  uint64_t t0 = 0;
   for (uint32_t i = 0; i < max_iters; ++i) {
     uint32_t done;
     asm volatile(
@@ -29,6 +39,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t addr, uint32_t parity, uint32
         : "r"(addr), "r"(parity)
         : "memory");
     if (done) return true;
+    if ((i & 63u) == 0) {  // read the clock now and then: it is not free
+      const uint64_t t = globaltimer_ns();
+      if (i == 0) {
+        t0 = t;
+      } else if (t - t0 > max_ns) {
+        return false;
+      }
+    }
   }
   return false;
 }

@@ -373,6 +373,9 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
   }
   cp_async_wait<0>();
   if (cur_b >= 0) finish(cur_b, e);
+  // the combine kernel (launched with programmatic stream serialization) may start its
+  // launch now; it still waits for this whole grid to finish before reading the partials
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -524,6 +527,9 @@ __global__ void __launch_bounds__(kCombWarps * 32) page16_decode_combine_kernel(
   __shared__ float s_red[kCombWarps];
   __shared__ float s_acc[kCombWarps][32];
   __shared__ int s_n;
+  // launched as a programmatic dependent of the decode kernel: wait until that grid has
+  // completed and its partials are visible (a no-op for an ordinary launch)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int b = blockIdx.x, hq = blockIdx.y;
   const int d0 = blockIdx.z * 32;  // this CTA's 32 head_dim columns
   const int64_t T_ = p.g_prefix[p.B];
@@ -688,7 +694,22 @@ int launch_mma(DecodeParams& p, cudaStream_t st) {
     return BPKV_ERR_CUDA;
   }
   kern<<<dim3(G, groups), NW * 32, smem, st>>>(p);
-  page16_decode_combine_kernel<T><<<dim3(p.B, p.Hq, (p.D + 31) / 32), kCombWarps * 32, 0, st>>>(p, G);
+  // the combine overlaps its launch with the decode grid's tail (programmatic dependent launch)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.B, p.Hq, (p.D + 31) / 32);
+  cfg.blockDim = dim3(kCombWarps * 32);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t le = cudaLaunchKernelEx(&cfg, page16_decode_combine_kernel<T>, p, G);
+  if (le != cudaSuccess) {
+    set_error("page16_native_launch:%s", cudaGetErrorString(le));
+    return BPKV_ERR_CUDA;
+  }
   BPKV_RETURN_LAUNCH("page16_native_launch");
 }
 

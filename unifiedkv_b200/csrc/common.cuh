@@ -151,4 +151,28 @@ __host__ __device__ __forceinline__ int64_t range_start(int c, int64_t T, int G)
   return (static_cast<int64_t>(c) * T) / G;
 }
 
+// ---- programmatic dependent launch ----------------------------------------
+// A kernel launched with launch_pdl may be launched while the previous kernel in
+// the stream is still running (its launch overlaps that kernel's tail).  It must
+// call pdl_wait() before touching any memory: that waits until the previous grid
+// has completed and its writes are visible.  For an ordinary launch pdl_wait()
+// returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
 }  // namespace bpkv

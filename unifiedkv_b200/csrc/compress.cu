@@ -252,6 +252,7 @@ __global__ void stats_reduce_kernel(const float2* ml_part, float2* ml, int nrows
 constexpr int kBlkPerCta = 14;  // (14 + 2) blocks x 16 tokens = 256 threads
 __global__ void __launch_bounds__(256) block_reduce_kernel(const float* headmax, float* out, int Hkv, int slots,
                                                            int Tm, int N, int smooth, int per_head) {
+  pdl_wait();
   __shared__ float raw[kBlkPerCta + 2];
   const int b0 = blockIdx.x * kBlkPerCta - 1;  // first (halo) block
   const int t = threadIdx.x;
@@ -325,6 +326,7 @@ __device__ int block_exclusive_scan(int local, int* wsum) {
 // order by an ordered compaction.
 __global__ void __launch_bounds__(1024) topk_select_kernel(const float* scores, int n, int k, int32_t* selected) {
   extern __shared__ __align__(128) uint8_t smem[];
+  pdl_wait();
   scores += static_cast<int64_t>(blockIdx.x) * n;  // one row of a batch per CTA
   selected += static_cast<int64_t>(blockIdx.x) * k;
   uint32_t* key = reinterpret_cast<uint32_t*>(smem);
@@ -422,6 +424,7 @@ __global__ void page_compact_kernel(const uint8_t* k_src, const uint8_t* v_src, 
                                     int obs, int eff_len, int Hkv, int row_bytes, int64_t src_sh_b,
                                     int64_t src_st_b, int64_t page_stride_b, int64_t dst_st_b, int64_t dst_sh_b,
                                     int64_t sel_stride_h) {
+  pdl_wait();
   const int j = blockIdx.x;  // destination page
   const bool is_v = blockIdx.y == 1;
   const uint8_t* src = is_v ? v_src : k_src;
@@ -543,7 +546,14 @@ int launch_score(ScoreParams& p, float* out, int N, int smooth, int per_head, cu
       // (pass 2 merges the per-range row statistics itself: no stats_reduce launch)
       rc = score_tc_pass(t, D, dt, 2, st);
       if (rc != BPKV_OK) return rc;
-      block_reduce_kernel<<<rgrid, 256, 0, st>>>(p.headmax, out, p.Hkv, t.hm_slots, p.Tm, N, smooth, per_head);
+      {
+        const cudaError_t le = launch_pdl(block_reduce_kernel, rgrid, dim3(256), 0, st, (const float*)p.headmax, out,
+                                          p.Hkv, t.hm_slots, p.Tm, N, smooth, per_head);
+        if (le != cudaSuccess) {
+          set_error("block_score_launch:%s", cudaGetErrorString(le));
+          return BPKV_ERR_CUDA;
+        }
+      }
       BPKV_RETURN_LAUNCH("block_score_launch");
     }
   }
@@ -684,7 +694,12 @@ extern "C" BPKV_API int bpkv_topk_select_batched(const float* scores, int n, int
     raised[dev] = true;
   }
   if (batch == 0) return BPKV_OK;
-  topk_select_kernel<<<batch, 1024, smem, static_cast<cudaStream_t>(stream)>>>(scores, n, k, selected);
+  const cudaError_t le = launch_pdl(topk_select_kernel, dim3(batch), dim3(1024), smem,
+                                    static_cast<cudaStream_t>(stream), scores, n, k, selected);
+  if (le != cudaSuccess) {
+    set_error("topk_select_launch:%s", cudaGetErrorString(le));
+    return BPKV_ERR_CUDA;
+  }
   BPKV_RETURN_LAUNCH("topk_select_launch");
 }
 
@@ -719,15 +734,15 @@ static int page_compact_impl(const void* k_src, const void* v_src, void* k_pool,
   const uint8_t *ks = static_cast<const uint8_t*>(k_src), *vs = static_cast<const uint8_t*>(v_src);
   uint8_t *kp = static_cast<uint8_t*>(k_pool), *vp = static_cast<uint8_t*>(v_pool);
   if (v16)
-    page_compact_kernel<uint4><<<grid, 256, 0, st>>>(ks, vs, kp, vp, selected, k_blocks, dst_pages, L, sink_len,
+    launch_pdl(page_compact_kernel<uint4>, grid, dim3(256), 0, st, ks, vs, kp, vp, selected, k_blocks, dst_pages, L, sink_len,
                                                      obs_len, eff_len, num_kv_heads, row_bytes, sh, stt, ps, dt, dh,
         sel_stride_h);
   else if (esz == 4)
-    page_compact_kernel<uint32_t><<<grid, 256, 0, st>>>(ks, vs, kp, vp, selected, k_blocks, dst_pages, L, sink_len,
+    launch_pdl(page_compact_kernel<uint32_t>, grid, dim3(256), 0, st, ks, vs, kp, vp, selected, k_blocks, dst_pages, L, sink_len,
                                                         obs_len, eff_len, num_kv_heads, row_bytes, sh, stt, ps, dt, dh,
         sel_stride_h);
   else
-    page_compact_kernel<uint16_t><<<grid, 256, 0, st>>>(ks, vs, kp, vp, selected, k_blocks, dst_pages, L, sink_len,
+    launch_pdl(page_compact_kernel<uint16_t>, grid, dim3(256), 0, st, ks, vs, kp, vp, selected, k_blocks, dst_pages, L, sink_len,
                                                         obs_len, eff_len, num_kv_heads, row_bytes, sh, stt, ps, dt, dh,
         sel_stride_h);
   BPKV_RETURN_LAUNCH("page_compact_launch");

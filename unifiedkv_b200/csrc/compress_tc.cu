@@ -108,6 +108,7 @@ __device__ __forceinline__ uint64_t exp2_sum32(const float* s, float scale, cons
 template <typename T, int PASS>
 __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_constant__ ScoreTcArgs args) {
   const ScoreTcParams& p = args.p;
+  pdl_wait();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* qs = smem;
@@ -436,7 +437,10 @@ int score_tc_pass(ScoreTcParams& p, int head_dim, int dtype, int pass, cudaStrea
       }                                                                                         \
       raised[v][dev] = true;                                                                    \
     }                                                                                           \
-    kern<<<grid, kThreads, kSmem, st>>>(args);                                                  \
+    if (launch_pdl(kern, grid, dim3(kThreads), kSmem, st, args) != cudaSuccess) {             \
+      set_error("block_score_tc_launch:launch");                                                \
+      return BPKV_ERR_CUDA;                                                                     \
+    }                                                                                           \
   } while (0)
   if (dtype == BPKV_BF16) {
     if (pass == 1) BPKV_SCORE_TC(__nv_bfloat16, 1); else BPKV_SCORE_TC(__nv_bfloat16, 2);

@@ -444,17 +444,25 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       tc::tc_fence_after();
       const int tbase = it * kBN + sc0;
       const bool crosses = tbase + kSC - 1 > lim;  // only tiles that cross this row's causal limit need the mask
-      // pass 1: row maximum over this thread's 64 columns (32 at a time; S is read again in pass 2)
+      // pass 1: row maximum over this thread's 64 columns; columns [32, 64) stay in registers for
+      // pass 2, which reads only [0, 32) again
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};  // four independent max chains
+      float s1[32];
       {
-        float s[kSC];
-        tc::tmem_ld32x2(ts, ts + 32, s, s + 32);
+        float s0[32];
+        tc::tmem_ld32x2(ts, ts + 32, s0, s1);
         if (crosses) {
 #pragma unroll
-          for (int c = 0; c < kSC; ++c) s[c] = (tbase + c <= lim) ? s[c] : -INFINITY;
+          for (int c = 0; c < 32; ++c) {
+            s0[c] = (tbase + c <= lim) ? s0[c] : -INFINITY;
+            s1[c] = (tbase + 32 + c <= lim) ? s1[c] : -INFINITY;
+          }
         }
 #pragma unroll
-        for (int c = 0; c < kSC; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+        for (int c = 0; c < 32; ++c) {
+          mx4[c & 3] = fmaxf(mx4[c & 3], s0[c]);
+          mx4[c & 3] = fmaxf(mx4[c & 3], s1[c]);
+        }
       }
       BPKV_MARK(1);
       const float mxh = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
@@ -475,29 +483,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         m_ref = mx;
         l_run *= alpha;
       }
-      if (it > 0 && __any_sync(0xffffffffu, need)) {
-#pragma unroll
-        for (int c0 = 0; c0 < kOC; c0 += 32) {
-          float o[32];
-          tc::tmem_ld32(to + c0, o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(to + c0, o);
-        }
-      }
       BPKV_MARK(4);
       const float m_use = m_ref == -INFINITY ? 0.f : m_ref;
       const uint64_t sc2 = pk2(p.scale_log2, p.scale_log2), nm2 = pk2(-m_use, -m_use);
       uint64_t sum2[2] = {0ull, 0ull};  // two independent packed sum chains (0ull = +0.0f pair)
-#pragma unroll
-      for (int c0 = 0; c0 < kSC; c0 += 32) {
-        // pass 2, chunk by chunk: S columns [c0, c0+32) -> P hi / lo in the same 32 columns
-        float s[32];
-        tc::tmem_ld32(ts + c0, s);
-        if (crosses) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) s[c] = (tbase + c0 + c <= lim) ? s[c] : -INFINITY;
-        }
+      // pass 2, chunk by chunk: S columns [c0, c0+32) -> P hi / lo in the same 32 columns; chunk
+      // [32, 64) first, from the registers of pass 1 (its P stores never touch columns [0, 32))
+      auto emit = [&](int c0, float* s) {
         uint32_t hi[16], lo[16];
 #pragma unroll
         for (int c = 0; c < 32; c += 2) {
@@ -529,8 +521,29 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         // P_g(it) over this chunk of S_g: token pair per 32-bit column, hi parts then lo parts
         tc::tmem_st16_nowait(ts + c0, hi);
         if (kBf16) tc::tmem_st16_nowait(ts + c0 + 16, lo);
+      };
+      emit(32, s1);
+      {
+        float s0[32];
+        tc::tmem_ld32(ts, s0);
+        if (crosses) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) s0[c] = (tbase + c <= lim) ? s0[c] : -INFINITY;
+        }
+        emit(0, s0);
       }
-      tc::tmem_st_wait();  // all P stores of this tile complete before the arrival below
+      // O rescale (rare: the reference max moved) after P, so S and O are not held together
+      if (it > 0 && __any_sync(0xffffffffu, need)) {
+#pragma unroll
+        for (int c0 = 0; c0 < kOC; c0 += 32) {
+          float o[32];
+          tc::tmem_ld32(to + c0, o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(to + c0, o);
+        }
+      }
+      tc::tmem_st_wait();  // all P (and O) stores of this tile complete before the arrival below
       BPKV_MARK(5);
       {
         float sa, sb;

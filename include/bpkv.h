@@ -161,10 +161,13 @@ BPKV_API int bpkv_lse_combine(const float* part_out, const float* part_lse, void
  * graph and replayed):
  *   bpkv_split_kv_merge_p2p: this rank's partial part_out [rows, head_dim]
  *   (dtype) with natural-log part_lse [rows] is stored into every rank's
- *   buffer over NVLink, a flag per rank marks it landed, then every rank
- *   waits for all flags of this epoch and writes the merged out [rows,
- *   head_dim] (and lse_out [rows] if not null).  A wait gives up after
- *   max_polls polls: *status is set to 1 and the rows are NaN.
+ *   buffer over NVLink as 16-byte words that carry the call number beside
+ *   each pair of values (no separate flag or fence), then every rank polls
+ *   the words of this call and writes the merged out [rows, head_dim] (and
+ *   lse_out [rows] if not null).  The launch is a programmatic dependent
+ *   launch: it may start during the grid that produced part_out and waits
+ *   for it.  A wait gives up after max_polls polls (or 4 s): *status is set
+ *   to 1 and the rows are NaN.
  * Teardown: bpkv_peer_buffer_close(bufs[r]) for r != rank, after a barrier
  * bpkv_peer_buffer_free(own).  world <= 8; head_dim % 4 == 0.  No multicast.
  * ------------------------------------------------------------------------ */

@@ -163,6 +163,65 @@ def test_p2p_merge_wait_runs_out_without_fault(cuda):
         L.bpkv_peer_buffer_free(fake_peer)
 
 
+def test_p2p_word_format_and_stale_words_one_gpu(cuda):
+    """The exchange words on one GPU, with no kernel waiting on another: rank 1 of a
+    two-rank group is emulated by writing its words for each call into rank 0's
+    buffer (torch ops) before rank 0's call.  A word is {x0, e, x1, e} (two fp32
+    values, each beside the call number e; the row's last word holds lse and 0),
+    at [e & 1][source rank][row][word].  Checks: the merge equals the log-sum-exp
+    merge of both partials; rank 0's own words land in the peer buffer in that
+    format; a word left over from call e-2 (same parity) is not taken for call e
+    (the wait runs out: status 1, NaN rows) and the next call works again."""
+    from unifiedkv_b200 import _lib
+    from oracle.page16 import lse_merge_reference
+    L = _lib.lib()
+    rows, d, world = 16, 128, 2
+    Wd = d // 2 + 1
+    nbytes = L.bpkv_peer_exchange_bytes(world, rows, d)
+    # plain device buffers stand in for the IPC-mapped ones (16-byte aligned, zeroed)
+    own = torch.zeros(nbytes // 4, dtype=torch.int32, device=cuda)
+    peer = torch.zeros_like(own)
+    n_words = 2 * world * rows * Wd * 4
+    own_w = own[:n_words].view(2, world, rows, Wd, 4)
+    peer_w = peer[:n_words].view(2, world, rows, Wd, 4)
+    g = torch.Generator(device=cuda).manual_seed(17)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    for call in (1, 2, 3, 4, 5):
+        par = call & 1
+        part0 = torch.randn(rows, d, generator=g, device=cuda).to(torch.bfloat16)
+        lse0 = torch.randn(rows, generator=g, device=cuda)
+        o1 = torch.randn(rows, d, generator=g, device=cuda)
+        lse1 = torch.randn(rows, generator=g, device=cuda)
+        emulate = call != 4  # call 4: rank 1 "never sends"; its parity slot holds call 2's words
+        if emulate:
+            vals = torch.cat([o1, torch.stack([lse1, torch.zeros_like(lse1)], 1)], 1).view(rows, Wd, 2)
+            own_w[par, 1, :, :, 0] = vals[..., 0].contiguous().view(torch.int32)
+            own_w[par, 1, :, :, 2] = vals[..., 1].contiguous().view(torch.int32)
+            own_w[par, 1, :, :, 1] = call
+            own_w[par, 1, :, :, 3] = call
+        out = torch.empty_like(part0)
+        lse_out = torch.empty(rows, device=cuda)
+        status.zero_()
+        _p2p_call(L, part0, lse0, [own.data_ptr(), peer.data_ptr()], 0, world, out, lse_out, status,
+                  1 << 20 if emulate else 5000)
+        torch.cuda.synchronize()
+        # rank 0's words in the peer's buffer, whatever happened to the wait
+        pw = peer_w[par, 0]
+        assert (pw[..., 1] == call).all() and (pw[..., 3] == call).all()
+        sent = torch.stack([pw[..., 0], pw[..., 2]], -1).contiguous().view(torch.float32).view(rows, 2 * Wd)
+        assert torch.equal(sent[:, :d], part0.float()) and torch.equal(sent[:, d], lse0)
+        if not emulate:
+            assert int(status.item()) == 1 and torch.isnan(out.float()).all() and torch.isnan(lse_out).all()
+            continue
+        assert int(status.item()) == 0
+        po = np.stack([part0.float().cpu().numpy(), o1.cpu().numpy()])
+        pl = np.stack([lse0.cpu().numpy(), lse1.cpu().numpy()])
+        ref_out, ref_lse = lse_merge_reference(po, pl)
+        err = np.abs(out.float().cpu().numpy() - ref_out) - 2.0 ** -8 * np.abs(ref_out)
+        assert err.max() < 1e-5
+        assert np.allclose(lse_out.cpu().numpy(), ref_lse, rtol=0, atol=1e-5)
+
+
 def _p2p_worker(rank, world, port, q_out):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))

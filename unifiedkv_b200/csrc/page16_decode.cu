@@ -530,6 +530,9 @@ __global__ void __launch_bounds__(kCombWarps * 32) page16_decode_combine_kernel(
   // launched as a programmatic dependent of the decode kernel: wait until that grid has
   // completed and its partials are visible (a no-op for an ordinary launch)
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  // a programmatic dependent (the NVLink merge of a split sequence) may become resident
+  // now; it waits for this grid's completion itself
+  asm volatile("griddepcontrol.launch_dependents;" :::);
   const int b = blockIdx.x, hq = blockIdx.y;
   const int d0 = blockIdx.z * 32;  // this CTA's 32 head_dim columns
   const int64_t T_ = p.g_prefix[p.B];

@@ -4,28 +4,30 @@
 //
 // Every rank owns one exchange buffer (cudaMalloc'd by this library, exported
 // to the other processes by CUDA IPC and mapped there once):
-//   float  data[2][world][rows][D + 4]     (out row, lse at column D; 16-B rows)
-//   uint32 flag[2][kMaxRanks]              (flag[par][r] = epoch: rank r's data landed)
-//   uint32 count[2][kMaxRanks]             (local: finished chunks per peer)
-//   uint32 epoch, merged                   (local: calls completed, merge CTAs done)
-// Call number e (kept in device memory, so the kernel can be captured in a CUDA
-// graph and replayed) uses parity e & 1: a peer may already write call
-// e+1 while this rank still merges e; e+2 cannot start before this rank has
-// finished e (its send of e+1 comes after).
+//   uint4  word[2][world][rows][D/2 + 1]   (parity, source rank, row)
+//   uint32 epoch, done                     (local: calls completed, CTAs done)
+// A word carries its own flag: {x0, e, x1, e} holds two fp32 values of the
+// row (out[2j], out[2j+1]; the last word holds lse and 0), each paired with
+// the call number e.  A 16-byte store reaches the peer as 8-byte pieces that
+// each land whole, so a reader that sees e in both flag slots of a word has
+// both of its values: no fence, counter or separate flag is needed, and the
+// exchange costs one NVLink store latency.  Call number e (kept in device
+// memory, so the kernel can be captured in a CUDA graph and replayed) uses
+// parity e & 1: a peer may already write call e+1 while this rank still
+// merges e; e+2 cannot start before this rank has finished e (the peer's
+// call e+1 needed this rank's e+1 words, which come after e).  A stale word
+// holds an older call number, so nothing is ever reset.
 //
-// peer_exchange_kernel<T>, one launch per call:
-//   1. CTA u = (peer index i, chunk c) stores chunk c of this rank's partial
-//      (T out, fp32 lse) into peer (rank + 1 + i) % world's buffer with plain
-//      stores through the IPC mapping (NVLink), fences at system scope, and
-//      the last chunk for that peer raises flag[par][rank] = e there with a
-//      release store.  The rank's own partial is not copied: the merge reads
-//      it in place.
-//   2. every CTA waits (bounded spin on acquire loads) until the flags of all
-//      other ranks for call e are up in the own buffer.  Those flags are set
-//      by the kernels of the other GPUs only, never by a CTA of this grid.
-//   3. the CTAs merge rows r = blockIdx.x*8 + warp, stride gridDim.x*8: M =
-//      max lse, W = sum exp(lse - M), out = sum exp(lse - M) o / W, lse_out =
-//      M + log W; the last CTA to finish advances the call number.
+// peer_exchange_kernel<T>, one launch per call, a programmatic dependent
+// launch of whatever produced the partial (it waits for that grid first):
+//   CTA c owns rows [8c, 8c+8).  It stores those rows of this rank's partial
+//   (T out converted to fp32, fp32 lse) into every peer's buffer with plain
+//   16-byte stores through the IPC mapping (NVLink), then merges them, one
+//   warp per row: the lse words of every other rank first (bounded spin on
+//   their call number), M = max lse, W = sum exp(lse - M), then out = sum
+//   exp(lse - M) o / W and lse_out = M + log W, each other rank's words read
+//   with the same bounded spin.  The own partial is read in place.  The last
+//   CTA to finish advances the call number.
 // A wait that runs out sets *status = 1 and writes NaN rows; the context stays
 // usable.  No multicast, no TMA: plain loads and stores.
 #include "common.cuh"
@@ -34,150 +36,152 @@ namespace bpkv {
 namespace {
 
 constexpr int kMaxRanks = 8;
-constexpr int kSendThreads = 256;
+constexpr int kRowsPerCta = 8;  // one merging warp per row
+constexpr int kThreads = kRowsPerCta * 32;
 
 struct PeerArgs {
-  float* bufs[kMaxRanks];  // every rank's exchange buffer as mapped in this process (own included)
+  uint4* bufs[kMaxRanks];  // every rank's exchange buffer as mapped in this process (own included)
   const void* part_out;    // [rows][D] this rank's partial output (T)
   const float* part_lse;   // [rows] natural-log sum-exp of this rank's partial
   void* out;               // [rows][D] merged output (T)
   float* lse_out;          // [rows] or null
   int* status;             // 0 ok, 1 a wait ran out
-  int rank, world, rows, D, chunks, rows_per_chunk;
+  int rank, world, rows, D;
   uint32_t max_polls;
 };
 
-__host__ __device__ inline int64_t row_floats(int D) { return D + 4; }
-__host__ __device__ inline int64_t data_floats(int world, int rows, int D) {
-  return 2LL * world * rows * row_floats(D);
+__host__ __device__ inline int64_t row_words(int D) { return D / 2 + 1; }
+__host__ __device__ inline int64_t data_words(int world, int rows, int D) { return 2LL * world * rows * row_words(D); }
+__device__ inline uint4* row_ptr(uint4* buf, const PeerArgs& a, int par, int src, int r) {
+  return buf + ((static_cast<int64_t>(par) * a.world + src) * a.rows + r) * row_words(a.D);
 }
-__device__ inline uint32_t* flag_ptr(float* buf, const PeerArgs& a, int par, int r) {
-  return reinterpret_cast<uint32_t*>(buf + data_floats(a.world, a.rows, a.D)) + par * kMaxRanks + r;
-}
-__device__ inline uint32_t* count_ptr(float* buf, const PeerArgs& a, int par, int p) {
-  return reinterpret_cast<uint32_t*>(buf + data_floats(a.world, a.rows, a.D)) + 2 * kMaxRanks + par * kMaxRanks + p;
-}
-__device__ inline uint32_t* epoch_ptr(float* buf, const PeerArgs& a) {
-  return reinterpret_cast<uint32_t*>(buf + data_floats(a.world, a.rows, a.D)) + 4 * kMaxRanks;
+__device__ inline uint32_t* epoch_ptr(uint4* buf, const PeerArgs& a) {
+  return reinterpret_cast<uint32_t*>(buf + data_words(a.world, a.rows, a.D));
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_volatile_v4(uint4* p, uint4 v) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint4 ld_volatile_v4(const uint4* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
-// One merged row, one warp.  Rank q's partial comes from the own buffer, the
-// own rank's from part_out / part_lse in place.
-template <typename T>
-__device__ void merge_row(const PeerArgs& a, const float* own, int par, int r, bool failed, int lane) {
-  T* out = reinterpret_cast<T*>(a.out) + static_cast<int64_t>(r) * a.D;
-  const float nan = __int_as_float(0x7fc00000);
-  if (failed) {
-    for (int d = lane; d < a.D; d += 32) out[d] = Elem<T>::from_f(nan);
-    if (a.lse_out != nullptr && lane == 0) a.lse_out[r] = nan;
-    return;
+// Spin until both flag slots of the word hold `epoch`; bounded by the poll budget
+// and by 4 s from t0.  Returns false (and leaves the word undefined) when it ran out.
+__device__ __forceinline__ bool wait_word(const uint4* p, uint32_t epoch, uint32_t& polls, uint32_t max_polls,
+                                          uint64_t t0, uint4& v) {
+  for (;;) {
+    v = ld_volatile_v4(p);
+    if (v.y == epoch && v.w == epoch) return true;
+    if (++polls > max_polls || ((polls & 63u) == 0u && now_ns() - t0 > 4000000000ull)) return false;
   }
-  const float* base = own + (static_cast<int64_t>(par) * a.world * a.rows + r) * row_floats(a.D);
-  const int64_t slot = static_cast<int64_t>(a.rows) * row_floats(a.D);
-  const T* mine = reinterpret_cast<const T*>(a.part_out) + static_cast<int64_t>(r) * a.D;
-  float lse[kMaxRanks];
-  float M = -INFINITY;
-#pragma unroll
-  for (int q = 0; q < kMaxRanks; ++q) {
-    lse[q] = q >= a.world ? -INFINITY : (q == a.rank ? a.part_lse[r] : base[q * slot + a.D]);
-    M = fmaxf(M, lse[q]);
-  }
-  if (M == -INFINITY) {  // no rank had keys for this row (the reference's 0/0)
-    for (int d = lane; d < a.D; d += 32) out[d] = Elem<T>::from_f(nan);
-    if (a.lse_out != nullptr && lane == 0) a.lse_out[r] = -INFINITY;
-    return;
-  }
-  float w[kMaxRanks];
-  float W = 0.f;
-#pragma unroll
-  for (int q = 0; q < kMaxRanks; ++q) {
-    w[q] = q < a.world ? expf(lse[q] - M) : 0.f;
-    W += w[q];
-  }
-  const float invW = 1.f / W;
-  for (int d = lane; d < a.D; d += 32) {
-    float acc = 0.f;
-#pragma unroll
-    for (int q = 0; q < kMaxRanks; ++q) {
-      if (q >= a.world || !(w[q] > 0.f)) continue;
-      acc += w[q] * (q == a.rank ? Elem<T>::to_f(mine[d]) : base[q * slot + d]);
-    }
-    out[d] = Elem<T>::from_f(acc * invW);
-  }
-  if (a.lse_out != nullptr && lane == 0) a.lse_out[r] = M + logf(W);
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kSendThreads) peer_exchange_kernel(const __grid_constant__ PeerArgs a) {
-  __shared__ int s_failed;
-  float* own = a.bufs[a.rank];
+__global__ void __launch_bounds__(kThreads) peer_exchange_kernel(const __grid_constant__ PeerArgs a) {
+  pdl_wait();  // the partial comes from the preceding grid
+  uint4* own = a.bufs[a.rank];
   const uint32_t epoch = *epoch_ptr(own, a) + 1u;  // this call; stored back by the last CTA below
   const int par = static_cast<int>(epoch & 1u);
-  const int n_send = (a.world - 1) * a.chunks;
-  // ---- 1. send ----
-  if (static_cast<int>(blockIdx.x) < n_send) {
-    const int i = blockIdx.x / a.chunks, c = blockIdx.x % a.chunks;
+  const int W = static_cast<int>(row_words(a.D)), H = a.D / 2;
+  const int r0 = blockIdx.x * kRowsPerCta, r1 = min(a.rows, r0 + kRowsPerCta);
+  const T* src = reinterpret_cast<const T*>(a.part_out);
+  // ---- 1. send this CTA's rows to every peer ----
+  const int n_words = (r1 - r0) * W;
+  for (int e = threadIdx.x; e < (a.world - 1) * n_words; e += blockDim.x) {
+    const int i = e / n_words, rem = e % n_words;
     const int p = (a.rank + 1 + i) % a.world;
-    float* dst = a.bufs[p] + ((static_cast<int64_t>(par) * a.world + a.rank) * a.rows) * row_floats(a.D);
-    const T* src = reinterpret_cast<const T*>(a.part_out);
-    const int r0 = c * a.rows_per_chunk, r1 = min(a.rows, r0 + a.rows_per_chunk);
-    const int q4 = a.D / 4;  // float4 per row (D % 4 == 0)
-    for (int e = threadIdx.x; e < (r1 - r0) * (q4 + 1); e += blockDim.x) {
-      const int r = r0 + e / (q4 + 1), j = e % (q4 + 1);
-      float* drow = dst + static_cast<int64_t>(r) * row_floats(a.D);
-      if (j < q4) {
-        const T* sp = src + static_cast<int64_t>(r) * a.D + 4 * j;
-        *reinterpret_cast<float4*>(drow + 4 * j) =
-            make_float4(Elem<T>::to_f(sp[0]), Elem<T>::to_f(sp[1]), Elem<T>::to_f(sp[2]), Elem<T>::to_f(sp[3]));
+    const int r = r0 + rem / W, j = rem % W;
+    float x0, x1;
+    if (j < H) {
+      x0 = Elem<T>::to_f(src[static_cast<int64_t>(r) * a.D + 2 * j]);
+      x1 = Elem<T>::to_f(src[static_cast<int64_t>(r) * a.D + 2 * j + 1]);
+    } else {
+      x0 = a.part_lse[r];
+      x1 = 0.f;
+    }
+    st_volatile_v4(row_ptr(a.bufs[p], a, par, a.rank, r) + j,
+                   make_uint4(__float_as_uint(x0), epoch, __float_as_uint(x1), epoch));
+  }
+  // ---- 2. merge, one warp per row ----
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = r0 + warp;
+  if (r < r1) {
+    T* out = reinterpret_cast<T*>(a.out) + static_cast<int64_t>(r) * a.D;
+    const T* mine = src + static_cast<int64_t>(r) * a.D;
+    const float nan = __int_as_float(0x7fc00000);
+    const uint64_t t0 = now_ns();
+    uint32_t polls = 0;
+    bool ok = true;
+    // lane q < world holds rank q's lse
+    float lq = -INFINITY;
+    if (lane < a.world) {
+      if (lane == a.rank) {
+        lq = a.part_lse[r];
       } else {
-        drow[a.D] = a.part_lse[r];
+        uint4 v;
+        ok = wait_word(row_ptr(own, a, par, lane, r) + H, epoch, polls, a.max_polls, t0, v);
+        lq = __uint_as_float(v.x);
       }
     }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();  // this chunk's stores before the count below
-      uint32_t* cnt = count_ptr(own, a, par, p);
-      if (atomicAdd(cnt, 1u) == static_cast<uint32_t>(a.chunks - 1)) {
-        *cnt = 0u;               // ready for call e + 2 (same parity)
-        __threadfence_system();  // every chunk's stores (seen through the count) before the flag
-        st_release_sys(flag_ptr(a.bufs[p], a, par, a.rank), epoch);
-      }
+    float wts[kMaxRanks];
+    float M = -INFINITY;
+    bool all_ok = __all_sync(0xffffffffu, ok);
+    if (all_ok) {
+#pragma unroll
+      for (int q = 0; q < kMaxRanks; ++q) M = fmaxf(M, __shfl_sync(0xffffffffu, lq, q));
     }
-  }
-  // ---- 2. wait for the other ranks' partials of this call ----
-  if (threadIdx.x == 0) {
-    int failed = 0;
-    for (int q = 0; q < a.world && !failed; ++q) {
-      if (q == a.rank) continue;
-      const uint32_t* f = flag_ptr(own, a, par, q);
-      uint32_t polls = 0;
-      uint64_t t0;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-      while (static_cast<int32_t>(ld_acquire_sys(f) - epoch) < 0) {
-        uint64_t t;
-        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-        if (++polls > a.max_polls || t - t0 > 4000000000ull) {  // poll count or 4 s, whichever first
-          failed = 1;
-          break;
+    float Wsum = 0.f;
+#pragma unroll
+    for (int q = 0; q < kMaxRanks; ++q) {
+      const float l = __shfl_sync(0xffffffffu, lq, q);
+      wts[q] = (q < a.world && M != -INFINITY) ? expf(l - M) : 0.f;
+      Wsum += wts[q];
+    }
+    if (all_ok && M != -INFINITY) {
+      const float invW = 1.f / Wsum;
+      for (int j = lane; j < H; j += 32) {
+        float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q) {
+          if (q >= a.world || !(wts[q] > 0.f)) continue;
+          float v0, v1;
+          if (q == a.rank) {
+            v0 = Elem<T>::to_f(mine[2 * j]);
+            v1 = Elem<T>::to_f(mine[2 * j + 1]);
+          } else {
+            uint4 v;
+            if (!wait_word(row_ptr(own, a, par, q, r) + j, epoch, polls, a.max_polls, t0, v)) ok = false;
+            v0 = __uint_as_float(v.x);
+            v1 = __uint_as_float(v.z);
+          }
+          acc0 += wts[q] * v0;
+          acc1 += wts[q] * v1;
         }
+        out[2 * j] = Elem<T>::from_f(acc0 * invW);
+        out[2 * j + 1] = Elem<T>::from_f(acc1 * invW);
       }
+      all_ok = __all_sync(0xffffffffu, ok);
+      if (all_ok && a.lse_out != nullptr && lane == 0) a.lse_out[r] = M + logf(Wsum);
+    } else if (all_ok) {  // no rank had keys for this row (the reference's 0/0)
+      for (int d = lane; d < a.D; d += 32) out[d] = Elem<T>::from_f(nan);
+      if (a.lse_out != nullptr && lane == 0) a.lse_out[r] = -INFINITY;
     }
-    s_failed = failed;
-    if (failed) atomicExch(a.status, 1);
+    if (!all_ok) {
+      for (int d = lane; d < a.D; d += 32) out[d] = Elem<T>::from_f(nan);
+      if (a.lse_out != nullptr && lane == 0) a.lse_out[r] = nan;
+      if (lane == 0) atomicExch(a.status, 1);
+    }
   }
-  __syncthreads();
-  // ---- 3. merge ----
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  for (int r = blockIdx.x * nw + warp; r < a.rows; r += gridDim.x * nw) merge_row<T>(a, own, par, r, s_failed != 0, lane);
   // the last CTA to finish advances the call number for the next call (every
   // CTA has read it by the time it counts itself done)
   __syncthreads();
@@ -198,7 +202,7 @@ using namespace bpkv;
 
 extern "C" BPKV_API size_t bpkv_peer_exchange_bytes(int world, int rows, int head_dim) {
   if (world <= 0 || world > kMaxRanks || rows <= 0 || head_dim <= 0) return 0;
-  return static_cast<size_t>(data_floats(world, rows, head_dim)) * sizeof(float) + (4 * kMaxRanks + 2) * sizeof(uint32_t);
+  return static_cast<size_t>(data_words(world, rows, head_dim)) * sizeof(uint4) + 4 * sizeof(uint32_t);
 }
 
 extern "C" BPKV_API int bpkv_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
@@ -266,7 +270,7 @@ extern "C" BPKV_API int bpkv_split_kv_merge_p2p(const void* part_out, const floa
   memset(&a, 0, sizeof(a));
   for (int r = 0; r < world; ++r) {
     BPKV_CHECK_ARG(peer_bufs[r] != nullptr && aligned16(peer_bufs[r]), "peer_exchange_shape:buffer_%d", r);
-    a.bufs[r] = static_cast<float*>(peer_bufs[r]);
+    a.bufs[r] = static_cast<uint4*>(peer_bufs[r]);
   }
   a.part_out = part_out;
   a.part_lse = part_lse;
@@ -277,16 +281,16 @@ extern "C" BPKV_API int bpkv_split_kv_merge_p2p(const void* part_out, const floa
   a.world = world;
   a.rows = rows;
   a.D = head_dim;
-  // about 8 chunks per peer (parallel stores), at most ~16 KB of rows each
-  a.rows_per_chunk = max(1, min((16384 / 4) / (head_dim + 4), (rows + 7) / 8));
-  a.chunks = (rows + a.rows_per_chunk - 1) / a.rows_per_chunk;
   a.max_polls = max_polls;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int grid = max((world - 1) * a.chunks, 1);
-#define BPKV_P2P(TY) peer_exchange_kernel<TY><<<grid, kSendThreads, 0, st>>>(a)
-  if (dtype == BPKV_BF16) BPKV_P2P(__nv_bfloat16);
-  else if (dtype == BPKV_F16) BPKV_P2P(__half);
-  else BPKV_P2P(float);
-#undef BPKV_P2P
+  const dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta);
+  cudaError_t le;
+  if (dtype == BPKV_BF16) le = launch_pdl(peer_exchange_kernel<__nv_bfloat16>, grid, dim3(kThreads), 0, st, a);
+  else if (dtype == BPKV_F16) le = launch_pdl(peer_exchange_kernel<__half>, grid, dim3(kThreads), 0, st, a);
+  else le = launch_pdl(peer_exchange_kernel<float>, grid, dim3(kThreads), 0, st, a);
+  if (le != cudaSuccess) {
+    set_error("split_kv_merge_p2p_launch:%s", cudaGetErrorString(le));
+    return BPKV_ERR_CUDA;
+  }
   BPKV_RETURN_LAUNCH("split_kv_merge_p2p_launch");
 }

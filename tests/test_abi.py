@@ -56,3 +56,55 @@ def test_new_entry_points_validate_without_gpu():
     rc = L.bpkv_page16_decode_append(None, None, None, 0, None, None, None, None, None, None, 2, 8, 2, 64, 1,
                                      0, 0, 0, 0, 0.1, 2, None, 0, None)
     assert rc == _lib.BPKV_ERR_SHAPE and "null_new_token" in _lib.last_error()
+
+
+def test_missing_library_fails_loudly():
+    """No CPU fallback: with the library missing, the reference's flag reads False and
+    every entry point raises (reference token page16_native_unavailable) instead of
+    computing anything.  Run in a fresh interpreter so the real library is not cached."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    code = r'''
+import torch
+from pathlib import Path
+import unifiedkv_b200._lib as L
+L.LIB_PATH = Path("/nonexistent/libbpkv.so")
+from unifiedkv_b200 import page16_native, compress, chunked_prefill, pool, varlen
+assert page16_native.HAS_TRITON is False and page16_native.HAS_PAGE16_NATIVE is False
+calls = {
+    "decode": lambda: page16_native.page16_decode_attention(
+        torch.zeros(1, 4, 64), torch.zeros(2, 16, 1, 64), torch.zeros(2, 16, 1, 64),
+        torch.zeros(1, 2, dtype=torch.int32), torch.ones(1, dtype=torch.int32), softmax_scale=0.125, n_rep=4),
+    "scores": lambda: compress.block_scores(torch.zeros(1, 64, 64), torch.zeros(4, 8, 64), 8, 8),
+    "topk": lambda: compress.topk_blocks(torch.zeros(10), 3),
+    "append": lambda: page16_native.decode_append(
+        torch.zeros(1, 1, 64), torch.zeros(1, 1, 64), torch.zeros(2, 16, 1, 64), torch.zeros(2, 16, 1, 64),
+        torch.zeros(1, 2, dtype=torch.int32), torch.zeros(1, dtype=torch.int32)),
+    "combine": lambda: page16_native.lse_combine(torch.zeros(2, 4, 64), torch.zeros(2, 4)),
+    "writeback": lambda: pool.write_pages(torch.zeros(4, 16, 1, 64), torch.zeros(4, 16, 1, 64),
+                                          torch.zeros(1, 64, 64), torch.zeros(1, 64, 64), [0, 1],
+                                          torch.zeros(1, dtype=torch.int32), 1, 16, 16),
+    "prefill": lambda: chunked_prefill.paged_chunk_prefill(
+        torch.zeros(4, 4, 64), torch.zeros(2, 16, 1, 64), torch.zeros(2, 16, 1, 64),
+        torch.zeros(1, 2, dtype=torch.int32), [0], [4], 0.125, 4),
+}
+for name, fn in calls.items():
+    try:
+        fn()
+    except RuntimeError as exc:
+        assert str(exc).startswith("page16_native_unavailable"), (name, str(exc))
+    else:
+        raise AssertionError(name + " ran without the library")
+try:  # the reference's varlen entry raises ImportError without its backend (core/varlen.py:4-9)
+    varlen.varlen_prefill_attention(torch.zeros(4, 4, 64), torch.zeros(4, 1, 64), torch.zeros(4, 1, 64), [4])
+except ImportError:
+    pass
+else:
+    raise AssertionError("varlen ran without the library")
+assert varlen.HAS_FLASH_ATTN is False
+print("ok")
+'''
+    root = Path(__file__).resolve().parents[1]
+    r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-3000:]

@@ -51,11 +51,12 @@ def paged_chunk_prefill(q_chunk: torch.Tensor, k_cache: torch.Tensor, v_cache: t
         max_q = max(chunk_lens, default=0)
     else:
         max_q = int(max_seqlen_q) if max_seqlen_q is not None else total
+    lib = _lib.lib()  # raises page16_native_unavailable when the library is missing
     q_chunk = q_chunk.contiguous()
     bt = block_table.to(torch.int32).contiguous()
     out = torch.empty_like(q_chunk)
     with torch.cuda.device(dev):
-        rc = _lib.lib().bpkv_paged_prefill(
+        rc = lib.bpkv_paged_prefill(
             q_chunk.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(), cu_seqlens_q.data_ptr(),
             seqlens_k.data_ptr(), out.data_ptr(), B, h_q, h_kv, d, int(bt.shape[1]), int(max_q), s[0], bt.stride(0),
             float(softmax_scale), int(bool(causal)), _lib.dtype_code(q_chunk.dtype), _lib.stream_ptr(dev))

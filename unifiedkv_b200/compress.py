@@ -78,9 +78,10 @@ def topk_blocks(scores: torch.Tensor, k: int) -> torch.Tensor:
     out = torch.empty((rows, k) if scores.dim() == 2 else (k,), dtype=torch.int32, device=scores.device)
     if k == 0 or rows == 0:
         return out
+    lib = _lib.lib()  # raises page16_native_unavailable when the library is missing
     s = scores.contiguous().float()
     with torch.cuda.device(s.device):
-        rc = _lib.lib().bpkv_topk_select_batched(s.data_ptr(), n, k, rows, out.data_ptr(), _lib.stream_ptr(s.device))
+        rc = lib.bpkv_topk_select_batched(s.data_ptr(), n, k, rows, out.data_ptr(), _lib.stream_ptr(s.device))
     _lib.check(rc, "topk_select")
     return out
 

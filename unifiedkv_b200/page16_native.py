@@ -167,8 +167,9 @@ def decode_append(k_new: torch.Tensor, v_new: torch.Tensor, k_cache: torch.Tenso
     bt = block_table.to(torch.int32).contiguous()
     lens = old_lens.to(torch.int32).contiguous()
     dev = k_new.device
+    lib = _lib.lib()  # raises page16_native_unavailable when the library is missing
     with torch.cuda.device(dev):
-        rc = _lib.lib().bpkv_decode_append(
+        rc = lib.bpkv_decode_append(
             k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), bt.data_ptr(),
             lens.data_ptr(), batch, h_kv, d, int(bt.shape[1]), k_new.stride(0), k_cache.stride(0), bt.stride(0),
             _lib.dtype_code(k_new.dtype), _lib.stream_ptr(dev))
@@ -183,8 +184,9 @@ def lse_combine(part_out: torch.Tensor, part_lse: torch.Tensor, out_dtype: torch
     part_lse = part_lse.contiguous().float()
     out = torch.empty(rows, d, dtype=out_dtype, device=part_out.device)
     lse = torch.empty(rows, dtype=torch.float32, device=part_out.device) if return_lse else None
+    lib = _lib.lib()  # raises page16_native_unavailable when the library is missing
     with torch.cuda.device(part_out.device):
-        rc = _lib.lib().bpkv_lse_combine(part_out.data_ptr(), part_lse.data_ptr(), out.data_ptr(), _lib.ptr(lse),
-                                         P, rows, d, _lib.dtype_code(out_dtype), _lib.stream_ptr(part_out.device))
+        rc = lib.bpkv_lse_combine(part_out.data_ptr(), part_lse.data_ptr(), out.data_ptr(), _lib.ptr(lse),
+                                  P, rows, d, _lib.dtype_code(out_dtype), _lib.stream_ptr(part_out.device))
     _lib.check(rc, "lse_combine")
     return (out, lse) if return_lse else out

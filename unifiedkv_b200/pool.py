@@ -193,16 +193,17 @@ def write_pages(k_dst: torch.Tensor, v_dst: torch.Tensor, K: torch.Tensor, V: to
         ps, st, sh = k_dst.stride(0), k_dst.stride(1), k_dst.stride(2)
     if k_dst.dtype != K.dtype:
         raise RuntimeError("selected_writeback_shape:dtype_mismatch")
+    lib = _lib.lib()  # raises page16_native_unavailable when the library is missing
     with torch.cuda.device(K.device):
         if selected is not None and selected.dim() == 2:
             if int(selected.shape[0]) != h_kv or selected.stride(1) != 1:
                 raise RuntimeError("selected_writeback_shape:per_kv_head_selected")
-            rc = _lib.lib().bpkv_page_compact_per_kv_head(
+            rc = lib.bpkv_page_compact_per_kv_head(
                 K.data_ptr(), V.data_ptr(), k_dst.data_ptr(), v_dst.data_ptr(), selected.data_ptr(),
                 selected.stride(0), int(k_blocks), dst_pages.data_ptr(), L, int(sink), int(obs), h_kv, d,
                 K.stride(0), K.stride(1), ps, st, sh, _lib.dtype_code(K.dtype), _lib.stream_ptr(K.device))
         else:
-            rc = _lib.lib().bpkv_page_compact(
+            rc = lib.bpkv_page_compact(
                 K.data_ptr(), V.data_ptr(), k_dst.data_ptr(), v_dst.data_ptr(), _lib.ptr(selected), int(k_blocks),
                 dst_pages.data_ptr(), L, int(sink), int(obs), h_kv, d, K.stride(0), K.stride(1), ps, st, sh,
                 _lib.dtype_code(K.dtype), _lib.stream_ptr(K.device))

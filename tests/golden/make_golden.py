@@ -1,8 +1,8 @@
 """Generates the golden fixtures in tests/golden/ from the REFERENCE itself.
 
-Run in a container where the reference tree is mounted (path from $BPKV_REFERENCE,
-default /root/reference); the fixtures are committed, the reference is never
-read at test time.
+Run where the reference tree is mounted (its path from $BPKV_REFERENCE, else the
+build container's mount point below); the fixtures are committed, the reference
+is never read at test time.
 
   * page16_*.npz  — outputs of the reference Triton kernel ``_page16_decode_kernel``
     (core/page16_native.py:17-80) executed by Triton's CPU interpreter

@@ -334,29 +334,73 @@ class AsyncOffloadManager:
         self._deferred_slots = keep
 
     # ---- decode bookkeeping (core/offload.py:780-866) -------------------------
+    def _evict_until_free(self, target_free: int, exclude_seq: int,
+                          protected_seqs: Optional[List[int]] = None) -> bool:
+        """Free pool pages by evicting whole sequences until ``target_free`` pages are
+        free (core/offload.py:257-287).  The victim choice is the engine's pressure
+        policy, supplied as ``evict_coldest_sequence(exclude_seq, protected_seqs=...)``
+        (returns the victim's id after starting its offload; raises MemoryError when
+        nothing can go); without one, nothing can be evicted."""
+        evict = getattr(self, "evict_coldest_sequence", None)
+        target = max(0, int(target_free))
+        while self.pool.n_free < target:
+            if evict is None:
+                return False
+            before = int(self.pool.n_free)
+            try:
+                victim = evict(exclude_seq, protected_seqs=protected_seqs)
+            except MemoryError:
+                return False
+            try:
+                self._try_finalize_offload(int(victim), force_sync=True)
+            except Exception:
+                return False
+            if int(self.pool.n_free) <= before and int(self.pool.n_free) < target:
+                self._inc_stat("evict_fail")
+                return False
+        return True
+
+    def _decode_fail(self, retryable: bool, reason: str) -> DecodeAppendResult:
+        self._inc_stat("decode_append_fail")
+        if retryable:
+            self._inc_stat("decode_append_retryable")
+        return DecodeAppendResult(ok=False, retryable=retryable, reason=reason)
+
     def reserve_decode_slot(self, seq_id: int) -> DecodeAppendResult:
-        entries = self._entries(seq_id)
-        if len(entries) != self.num_layers:
-            return DecodeAppendResult(ok=False, retryable=False, reason=f"missing_page_table_entry seq={seq_id}")
+        """Make room for one decode token of a fully resident sequence: a new page
+        (the same id in every layer) when the last page is full.  Same checks,
+        order, reasons and stats as the reference."""
+        entries = [self.page_table.get((seq_id, l)) for l in range(self.num_layers)]
+        if any(e is None for e in entries):
+            return self._decode_fail(False, f"missing_page_table_entry seq={seq_id}")
         for e in entries:
             self._ensure_entry_maps(e)
-            if e.state != OffloadState.ON_GPU or any(int(b) < 0 for b in e.gpu_block_map):
-                return DecodeAppendResult(ok=False, retryable=True,
-                                          reason=f"direct_decode_not_on_gpu seq={seq_id} state={e.state}")
+            if e.state != OffloadState.ON_GPU:
+                return self._decode_fail(True, f"direct_decode_not_on_gpu seq={seq_id} state={e.state}")
+            if any(int(b) < 0 for b in e.gpu_block_map):
+                return self._decode_fail(True, f"direct_decode_resident_missing seq={seq_id}")
+            if not e.block_ids:
+                self._inc_stat("decode_append_fail")
+                return DecodeAppendResult(ok=False, retryable=True, reason=f"direct_decode_no_gpu_blocks seq={seq_id}")
         seq_len = int(entries[0].seq_len)
         if any(int(e.seq_len) != seq_len for e in entries):
-            return DecodeAppendResult(ok=False, retryable=False,
-                                      reason=f"direct_decode_inconsistent_seq_len seq={seq_id}")
+            return self._decode_fail(False, f"direct_decode_inconsistent_seq_len seq={seq_id}")
         if seq_len % self.pool.B == 0:
             new = self.pool.allocate_blocks(1)
             if not new:
-                return DecodeAppendResult(ok=False, retryable=True, reason="direct_decode_expand_alloc_failed")
+                if not self._evict_until_free(max(self.pool.N_wm_high, 1), seq_id, protected_seqs=[seq_id]):
+                    return self._decode_fail(True, "direct_decode_expand_evict_failed")
+                new = self.pool.allocate_blocks(1)
+                if not new:
+                    return self._decode_fail(True, "direct_decode_expand_alloc_failed")
             for e in entries:
+                self._ensure_entry_maps(e)
                 e.block_ids.append(int(new[0]))
                 e.gpu_block_map.append(int(new[0]))
                 e.cpu_k_blocks.append(None)
                 e.cpu_v_blocks.append(None)
                 e.materialized_blocks = len(e.gpu_block_map)
+                self._update_entry_state(e)
         return DecodeAppendResult(ok=True)
 
     def commit_decode_token(self, seq_id: int) -> None:

@@ -32,3 +32,22 @@ def test_block_table_is_zero_padded_int32():
     assert t.dtype == torch.int32
     assert t.tolist() == [[3, 4, 9], [7, 0, 0], [0, 0, 0]]
     assert block_table_tensor([[], []], torch.device("cpu")).shape == (2, 0)
+
+
+def test_token_writes_and_page_reads():
+    """write_one_token (core/pool.py:143-152) and read_kv_from_blocks (:154-172):
+    tokens written at (page, slot) read back in sequence order across pages,
+    the partial last page cut at seq_len, and an empty read shaped [h_kv, 0, d]."""
+    pool = PagedKVPool(16, 2, 2, 8, torch.float32, device="cpu", n_total=12)
+    pages = [7, 2, 9]
+    K = torch.randn(2, 40, 8)
+    V = torch.randn(2, 40, 8)
+    for t in range(40):
+        pool.write_one_token(1, pages[t // 16], t % 16, K[:, t:t + 1], V[:, t:t + 1])
+    k, v = pool.read_kv_from_blocks(1, pages, 40)
+    assert k.shape == (2, 40, 8) and torch.equal(k, K) and torch.equal(v, V)
+    k, v = pool.read_kv_from_blocks(1, pages, 20)
+    assert torch.equal(k, K[:, :20]) and torch.equal(v, V[:, :20])
+    assert torch.count_nonzero(pool.k_cache[0]) == 0  # the other layer is untouched
+    k, v = pool.read_kv_from_blocks(1, [], 5)
+    assert k.shape == (2, 0, 8) and v.shape == (2, 0, 8)

@@ -106,3 +106,67 @@ def test_split_kv_exchange_gloo(world):
     assert res[0][2] == {10: 1, 11: 1, 12: 0}
     # rank 1 (10-page pool, 8 used) is at 20% free: every rank sees the global minimum
     assert res[0][3] == res[1][3] == "WARNING"
+
+
+def test_coordinator_register_append_evict_release():
+    """The reference's coordinator calls (core/multi_gpu.py:61-123) on one rank over a
+    CPU pool: registration allocates the shared pages once, head shards go back
+    together, decode tokens land at each layer's length with layer 0 taking the new
+    page, another rank's requests are not stored, eviction reaches the offloader's
+    policy, release frees everything.  The page write of a whole layer is the copy
+    kernel on a GPU; a torch restatement of the reference's page loop stands in here."""
+    coord = MultiGPUCoordinator(1, 16, 2, 4, 8, torch.float32, device=torch.device("cpu"), n_pages=20)
+    pool = coord.pool
+
+    def write_kv_to_blocks(layer_id, block_ids, K, V):  # core/pool.py:127-142
+        for i, bid in enumerate(block_ids):
+            s, e = 16 * i, min(16 * i + 16, K.shape[1])
+            if e > s:
+                pool.k_cache[layer_id, bid, :e - s] = K[:, s:e].transpose(0, 1)
+                pool.v_cache[layer_id, bid, :e - s] = V[:, s:e].transpose(0, 1)
+
+    pool.write_kv_to_blocks = write_kv_to_blocks
+    assert coord.assign({5: 40, 6: 10}) == {5: 0, 6: 0}
+    g = torch.Generator().manual_seed(0)
+    K = [torch.randn(4, 40, 8, generator=g) for _ in range(2)]
+    V = [torch.randn(4, 40, 8, generator=g) for _ in range(2)]
+    assert coord.register_layer_from_full_kv(5, 0, K[0], V[0])
+    ids = list(coord.local_blocks[5])
+    assert len(ids) == 3 and pool.n_free == 17
+    shards = [(K[1][:2], V[1][:2]), (K[1][2:], V[1][2:])]  # the reference's per-GPU head shards
+    assert coord.register_all_gpus(5, 1, shards) and coord.local_blocks[5] == ids and pool.n_free == 17
+    toks = [[(torch.randn(4, 1, 8, generator=g), torch.randn(4, 1, 8, generator=g)) for _ in range(2)]
+            for _ in range(10)]
+    for step in toks:  # positions 40..49: the page boundary at 48 is crossed by layer 0 first
+        for layer, (kt, vt) in enumerate(step):
+            assert coord.append_decode_token_all_gpus(5, layer, kt, vt)
+    assert len(coord.local_blocks[5]) == 4 and pool.n_free == 16
+    for layer in range(2):
+        kb, vb = pool.read_kv_from_blocks(layer, coord.local_blocks[5], 50)
+        want_k = torch.cat([K[layer]] + [toks[t][layer][0] for t in range(10)], dim=1)
+        want_v = torch.cat([V[layer]] + [toks[t][layer][1] for t in range(10)], dim=1)
+        assert torch.equal(kb, want_k) and torch.equal(vb, want_v)
+        assert coord.seq_lens[(5, layer)] == 50
+    # a layer other than 0 reaching a full last page first has no page to write into
+    for _ in range(14):
+        coord.append_decode_token_all_gpus(5, 1, *toks[0][1])
+    with pytest.raises(RuntimeError, match="multi_gpu_append_without_page seq=5 layer=1"):
+        coord.append_decode_token_all_gpus(5, 1, *toks[0][1])
+    # another rank's request: nothing stored here
+    coord.owner[7] = 1
+    assert not coord.register_layer_from_full_kv(7, 0, K[0], V[0])
+    assert not coord.append_decode_token_all_gpus(7, 0, *toks[0][0])
+    # eviction goes to the offloader's policy; MemoryError (nothing to evict) is absorbed
+    coord.global_evict(0, 5)  # no offloader: nothing happens
+    calls = []
+
+    class Off:
+        def evict_coldest_sequence(self, seq):
+            calls.append(seq)
+            raise MemoryError
+
+    coord.offloader = Off()
+    coord.global_evict(3, 5)
+    assert calls == [5]
+    coord.release_all(5)
+    assert pool.n_free == 20 and not any(k[0] == 5 for k in coord.seq_lens) and 5 not in coord.owner

@@ -205,6 +205,8 @@ class MultiGPUCoordinator:
                                 gpu_mem_frac=0.9, cpu_mem_gb=cpu_mem_gb_per_gpu, device=self.device, n_total=n_pages)
         self.owner: Dict[int, int] = {}
         self.local_blocks: Dict[int, List[int]] = {}
+        self.seq_lens: Dict[Tuple[int, int], int] = {}  # (seq, layer) -> tokens stored on this rank
+        self.offloader = None  # optional, with the engine's evict_coldest_sequence policy
 
     def assign(self, seq_lens: Dict[int, int]) -> Dict[int, int]:
         """Shard new requests {seq_id: length} over ranks; returns {seq_id: rank}."""
@@ -226,6 +228,72 @@ class MultiGPUCoordinator:
         self.local_blocks.setdefault(int(seq_id), []).extend(ids)
         return ids
 
+    def _split_kv_heads(self, K: torch.Tensor, V: torch.Tensor) -> List[Tuple[torch.Tensor, torch.Tensor]]:
+        """The reference cuts K/V [h_kv_total, ...] into per-GPU head ranges
+        (core/multi_gpu.py:49-59); a rank here holds every head of its own
+        requests, so there is one shard: all heads."""
+        return [(K.contiguous(), V.contiguous())]
+
+    def register_layer_from_full_kv(self, seq_id: int, layer_id: int, K: torch.Tensor, V: torch.Tensor) -> bool:
+        """One layer of a prefilled sequence, K/V [h_kv_total, L, d] (core/multi_gpu.py:76-84).
+
+        Only the owning rank stores it; the first layer registered allocates the
+        ceil(L/16) pages that every layer of the sequence shares.  Returns
+        whether this rank stored it."""
+        if not self.is_local(seq_id):
+            return False
+        L = int(K.shape[1])
+        need = (L + self.pool.B - 1) // self.pool.B
+        ids = self.local_blocks.get(int(seq_id))
+        if ids is None:
+            ids = self.allocate(seq_id, need)
+        elif len(ids) < need:
+            raise RuntimeError(f"multi_gpu_layer_len_mismatch seq={seq_id} layer={layer_id} len={L} pages={len(ids)}")
+        self.pool.write_kv_to_blocks(int(layer_id), list(ids), K, V)
+        self.seq_lens[(int(seq_id), int(layer_id))] = L
+        return True
+
+    def register_all_gpus(self, seq_id: int, layer_id: int, kv_shards: List[Tuple[torch.Tensor, torch.Tensor]]) -> bool:
+        """The reference's per-GPU head shards of one layer (core/multi_gpu.py:61-74),
+        put back together: this rank's pool holds every head."""
+        K = torch.cat([k for k, _ in kv_shards], dim=0)
+        V = torch.cat([v for _, v in kv_shards], dim=0)
+        return self.register_layer_from_full_kv(seq_id, layer_id, K, V)
+
+    def append_decode_token_all_gpus(self, seq_id: int, layer_id: int, k_tok: torch.Tensor,
+                                     v_tok: torch.Tensor) -> bool:
+        """This step's token of one layer, k_tok/v_tok [h_kv_total, 1, d]
+        (core/multi_gpu.py:86-102).  The owning rank stores it at position
+        seq_len of that layer; layer 0 takes a new page (shared by all layers)
+        when the last one is full, as core/offload.py:926-951 does.  Returns
+        whether this rank stored it."""
+        if not self.is_local(seq_id):
+            return False
+        key = (int(seq_id), int(layer_id))
+        n = self.seq_lens.get(key, 0)
+        ids = self.local_blocks.get(int(seq_id), [])
+        if n >= len(ids) * self.pool.B:
+            if int(layer_id) != 0:
+                raise RuntimeError(f"multi_gpu_append_without_page seq={seq_id} layer={layer_id}")
+            self.allocate(seq_id, 1)
+            ids = self.local_blocks[int(seq_id)]
+        self.pool.write_one_token(int(layer_id), ids[n // self.pool.B], n % self.pool.B, k_tok, v_tok)
+        self.seq_lens[key] = n + 1
+        return True
+
+    def global_evict(self, current_layer: int, current_seq: int) -> None:
+        """Ask this rank's offloader to evict its coldest sequence (core/multi_gpu.py:104-110);
+        the world-wide view is each rank doing the same.  No offloader with a
+        policy: nothing to evict."""
+        del current_layer
+        evict = getattr(self.offloader, "evict_coldest_sequence", None)
+        if evict is None:
+            return
+        try:
+            evict(current_seq)
+        except MemoryError:
+            pass
+
     def global_watermark(self) -> str:
         """Worst free ratio over ranks (core/multi_gpu.py:112-119 thresholds)."""
         ratio = self.pool.n_free / max(1, self.pool.N_total)
@@ -245,3 +313,5 @@ class MultiGPUCoordinator:
         if ids:
             self.pool.free_blocks_by_ids(ids)
         self.owner.pop(int(seq_id), None)
+        for key in [k for k in self.seq_lens if k[0] == int(seq_id)]:
+            del self.seq_lens[key]

@@ -101,6 +101,72 @@ class AsyncOffloadManager:
                     gpu_block_map=list(block_ids), cpu_k_blocks=[None] * len(block_ids),
                     cpu_v_blocks=[None] * len(block_ids))
 
+    def register(self, seq_id: int, layer_id: int, K: torch.Tensor, V: torch.Tensor) -> List[int]:
+        """One layer of a prefilled sequence, K/V [h_kv, L, d], into fresh pages
+        (core/offload.py:451-473).  Returns the page ids."""
+        seq_len = int(K.shape[1])
+        n_blocks = (seq_len + self.pool.B - 1) // self.pool.B
+        block_ids = self.pool.allocate_blocks(n_blocks)
+        if not block_ids:
+            raise MemoryError(f"GPU blocks exhausted: seq={seq_id} layer={layer_id}")
+        self.pool.write_kv_to_blocks(int(layer_id), block_ids, K, V)
+        with self.lock:
+            self.page_table[(int(seq_id), int(layer_id))] = BlockTableEntry(
+                seq_id=int(seq_id), layer_id=int(layer_id), state=OffloadState.ON_GPU, block_ids=list(block_ids),
+                seq_len=seq_len, logical_seq_len=seq_len, materialized_blocks=len(block_ids),
+                gpu_block_map=list(block_ids), cpu_k_blocks=[None] * n_blocks, cpu_v_blocks=[None] * n_blocks)
+        self._mark_resident(int(seq_id))
+        return list(block_ids)
+
+    def register_all_layers(self, seq_id: int, block_ids: List[int], seq_len: int, K_list: list, V_list: list,
+                            anchor_k_means: Optional[list] = None, logical_seq_len: Optional[int] = None) -> None:
+        """Every layer of a sequence into the same, already allocated pages
+        (core/offload.py:475-510); a layer whose K is None is skipped."""
+        logical = int(seq_len if logical_seq_len is None else logical_seq_len)
+        for layer_id, (K, V) in enumerate(zip(K_list, V_list)):
+            if K is None:
+                continue
+            anchor = anchor_k_means[layer_id] if anchor_k_means is not None and layer_id < len(anchor_k_means) else None
+            if torch.is_tensor(anchor):
+                anchor = anchor.detach().cpu()
+            self.pool.write_kv_to_blocks(layer_id, list(block_ids), K, V)
+            with self.lock:
+                self.page_table[(int(seq_id), layer_id)] = BlockTableEntry(
+                    seq_id=int(seq_id), layer_id=layer_id, state=OffloadState.ON_GPU, block_ids=list(block_ids),
+                    seq_len=int(seq_len), logical_seq_len=logical, materialized_blocks=len(block_ids),
+                    prefill_anchor_k_mean=anchor, gpu_block_map=list(block_ids),
+                    cpu_k_blocks=[None] * len(block_ids), cpu_v_blocks=[None] * len(block_ids))
+        self._mark_resident(int(seq_id))
+
+    def _sequence_has_state(self, seq_id: int, state: OffloadState) -> bool:
+        return any(e.state == state for e in self._entries(seq_id))
+
+    def get_sequence_residency(self, seq_id: int) -> Dict[str, int]:
+        """Residency summary with the reference's keys (core/offload.py:307-360).
+        No residency-protection policy runs here, so residency_protected is 0."""
+        entries = self._entries(seq_id)
+        if not entries:
+            return dict(exists=0, on_gpu=0, resident_blocks=0, logical_blocks=0, materialized_blocks=0,
+                        resident_ratio_x1000=0, has_cpu_blocks=0, state_mixed=0, last_access=-1,
+                        residency_protected=0)
+        resident = logical = materialized = 0
+        on_gpu = has_cpu = mixed = 0
+        last_access = -1
+        for e in entries:
+            self._ensure_entry_maps(e)
+            resident = max(resident, sum(1 for b in e.gpu_block_map if int(b) >= 0))
+            materialized = max(materialized, int(e.materialized_blocks or len(e.gpu_block_map)))
+            n_tok = int(e.logical_seq_len or e.seq_len or 0)
+            logical = max(logical, (n_tok + self.pool.B - 1) // self.pool.B)
+            on_gpu |= int(e.state == OffloadState.ON_GPU)
+            mixed |= int(e.state == OffloadState.MIXED)
+            has_cpu |= int(any(x is not None for x in e.cpu_k_blocks))
+            last_access = max(last_access, int(getattr(e, "last_access", -1)))
+        return dict(exists=1, on_gpu=on_gpu, resident_blocks=resident, logical_blocks=logical,
+                    materialized_blocks=materialized,
+                    resident_ratio_x1000=int(1000 * resident / max(1, materialized)) if materialized > 0 else 0,
+                    has_cpu_blocks=has_cpu, state_mixed=mixed, last_access=last_access, residency_protected=0)
+
     def _flat_ids(self, pages: List[int]) -> torch.Tensor:
         """Flat [L*N] pool page indices, page-major: entry j*L + l is page j of layer l."""
         N = self.pool.N_total
@@ -224,6 +290,41 @@ class AsyncOffloadManager:
         return True
 
     # ---- prefetch (pinned host -> device) ------------------------------------
+    def _host_resident(self, seq_id: int, logical_block_indices: List[int]) -> List[int]:
+        """The requested logical pages that live in host slots, ascending."""
+        entries = self._entries(seq_id)
+        if not entries:
+            return []
+        first = entries[0]
+        return sorted({int(i) for i in logical_block_indices
+                       if 0 <= int(i) < len(first.gpu_block_map) and int(first.gpu_block_map[int(i)]) < 0
+                       and (seq_id, int(i)) in self._slot_of})
+
+    def prefetch_sequence(self, seq_id: int) -> bool:
+        """Every host-resident page of the sequence back to the pool
+        (core/offload.py:693-706); waits for the copy if it could not finish at once."""
+        entries = self._entries(seq_id)
+        if not entries:
+            self._inc_stat("prefetch_noop")
+            self._inc_stat("prefetch_success")
+            return True
+        n = max(len(e.gpu_block_map) for e in entries)
+        ok = self.prefetch_sequence_blocks(seq_id, list(range(n)))
+        if not ok:
+            ok = self._try_finalize_prefetch(seq_id, force_sync=True)
+        return bool(ok)
+
+    def ensure_sequence_on_gpu(self, seq_id: int, allow_evict: bool = True,
+                               protected_seqs: Optional[List[int]] = None) -> bool:
+        """All pages of the sequence resident (core/offload.py:759-778)."""
+        entries = self._entries(seq_id)
+        if not entries:
+            self._inc_stat("ensure_fail")
+            return False
+        n = max(len(e.gpu_block_map) for e in entries)
+        return self.ensure_sequence_blocks_on_gpu(seq_id, list(range(n)), allow_evict=allow_evict,
+                                                  protected_seqs=protected_seqs)
+
     def prefetch_sequence_blocks(self, seq_id: int, logical_block_indices: List[int]) -> bool:
         """Start copying host-resident pages back into fresh pool pages.  Returns
         True when nothing is left to fetch, False while a transfer is in flight
@@ -238,10 +339,7 @@ class AsyncOffloadManager:
         if not entries:
             self._inc_stat('prefetch_noop')
             return True
-        first = entries[0]
-        sel = sorted({int(i) for i in logical_block_indices
-                      if 0 <= int(i) < len(first.gpu_block_map) and int(first.gpu_block_map[int(i)]) < 0
-                      and (seq_id, int(i)) in self._slot_of})
+        sel = self._host_resident(seq_id, logical_block_indices)
         if not sel:
             self._inc_stat('prefetch_noop')
             return True
@@ -299,17 +397,26 @@ class AsyncOffloadManager:
         self._apply_prefetch(seq_id, p)
         return True
 
-    def ensure_sequence_blocks_on_gpu(self, seq_id: int, logical_block_indices: Optional[List[int]] = None,
+    def ensure_sequence_blocks_on_gpu(self, seq_id: int, missing_block_indices: Optional[List[int]] = None,
+                                      allow_evict: bool = True, protected_seqs: Optional[List[int]] = None,
                                       stream: Optional[torch.cuda.Stream] = None) -> bool:
         """Make the given pages resident for work queued on ``stream`` (default:
         the current stream) WITHOUT blocking the host: the prefetch runs on the
         side stream and ``stream`` waits on its event.  Host slots are recycled
-        when the event has completed (polled by later calls)."""
+        when the event has completed (polled by later calls).  Parameters as in
+        core/offload.py:708-757: with ``allow_evict``, a pool short of pages
+        first evicts other sequences through the engine's policy (if one is
+        attached; ``protected_seqs`` and this sequence are never chosen)."""
+        self._inc_stat("ensure_calls")
         self._try_finalize_offload(seq_id, force_sync=True)
         entries = self._entries(seq_id)
         if not entries:
             return False
-        idx = list(range(len(entries[0].gpu_block_map))) if logical_block_indices is None else logical_block_indices
+        idx = list(range(len(entries[0].gpu_block_map))) if missing_block_indices is None else missing_block_indices
+        if allow_evict and seq_id not in self._pending:
+            need = len(self._host_resident(seq_id, idx))
+            if need > self.pool.n_free:
+                self._evict_until_free(need, seq_id, protected_seqs=[int(seq_id)] + list(protected_seqs or []))
         if self.prefetch_sequence_blocks(seq_id, idx):
             return True
         p = self._pending.get(seq_id)
@@ -401,6 +508,64 @@ class AsyncOffloadManager:
                 e.cpu_v_blocks.append(None)
                 e.materialized_blocks = len(e.gpu_block_map)
                 self._update_entry_state(e)
+        return DecodeAppendResult(ok=True)
+
+    def append_decode_token(self, seq_id: int, layer_id: int, k_tok: torch.Tensor,
+                            v_tok: torch.Tensor) -> DecodeAppendResult:
+        """Store one layer's decode token, k_tok/v_tok [h_kv, 1, d], at position
+        seq_len of that layer (core/offload.py:868-960): a non-resident sequence is
+        brought back first, layer 0 takes a new page (for every layer) when the
+        last one is full.  Same reasons and stats as the reference.  The batched
+        decode path uses reserve_decode_slot + the fused append of the decode
+        launch instead."""
+        self._inc_stat("decode_append_calls")
+        key = (int(seq_id), int(layer_id))
+        entry = self.page_table.get(key)
+        if entry is None:
+            return self._decode_fail(False, f"missing_page_table_entry seq={seq_id} layer={layer_id}")
+        self._ensure_entry_maps(entry)
+        if entry.state != OffloadState.ON_GPU or any(int(b) < 0 for b in entry.gpu_block_map):
+            # True from ensure means the page map is valid in stream order (the copy may still run)
+            ok = self.ensure_sequence_on_gpu(seq_id, allow_evict=True, protected_seqs=[seq_id])
+            if not ok or any(int(b) < 0 for b in entry.gpu_block_map):
+                reason = f"prefetch_before_decode_append_failed seq={seq_id}"
+                if self._sequence_has_state(seq_id, OffloadState.PREFETCH_INFLIGHT):
+                    reason = f"prefetch_inflight seq={seq_id}"
+                elif self._sequence_has_state(seq_id, OffloadState.OFFLOAD_INFLIGHT):
+                    reason = f"offload_inflight seq={seq_id}"
+                return self._decode_fail(True, reason)
+            entry = self.page_table.get(key)
+            if entry is None:
+                return self._decode_fail(False, f"missing_page_table_after_prefetch seq={seq_id} layer={layer_id}")
+        self._ensure_entry_maps(entry)
+        if not entry.block_ids:
+            self._inc_stat("decode_append_fail")
+            return DecodeAppendResult(ok=False, retryable=True,
+                                      reason=f"no_gpu_blocks_for_decode_append seq={seq_id} layer={layer_id}")
+        last_used = int(entry.seq_len) % self.pool.B
+        if last_used == 0 and int(layer_id) == 0:
+            new = self.pool.allocate_blocks(1)
+            if not new:
+                if not self._evict_until_free(max(self.pool.N_wm_high, 1), seq_id, protected_seqs=[seq_id]):
+                    return self._decode_fail(True, "decode_expand_evict_failed")
+                new = self.pool.allocate_blocks(1)
+                if not new:
+                    return self._decode_fail(True, "decode_expand_alloc_failed")
+            for e in self._entries(seq_id):
+                self._ensure_entry_maps(e)
+                e.block_ids.append(int(new[0]))
+                e.gpu_block_map.append(int(new[0]))
+                e.cpu_k_blocks.append(None)
+                e.cpu_v_blocks.append(None)
+                e.materialized_blocks = len(e.gpu_block_map)
+                self._update_entry_state(e)
+        self.pool.write_one_token(int(layer_id), int(entry.block_ids[-1]), last_used, k_tok, v_tok)
+        if int(entry.logical_seq_len or 0) <= 0:
+            entry.logical_seq_len = int(entry.seq_len)
+        entry.seq_len += 1
+        entry.logical_seq_len += 1
+        entry.materialized_blocks = max(int(entry.materialized_blocks or 0), len(entry.gpu_block_map))
+        self._inc_stat("decode_append_success")
         return DecodeAppendResult(ok=True)
 
     def commit_decode_token(self, seq_id: int) -> None:

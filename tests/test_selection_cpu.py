@@ -1,4 +1,5 @@
-"""CPU tests of the selected-writeback host logic (no kernel runs): the
+"""CPU tests of the selected-writeback host logic (no kernel runs): the budget
+rules against the reference's own table and the oracle, the
 transaction's rollback (core/scheduler.py:805-878), the writeback allocation
 with watermark eviction (core/scheduler.py:654-664) and its failure mode.
 A CPU-device pool exercises the allocator; every case below fails or returns
@@ -63,3 +64,32 @@ def test_watermark_eviction_before_allocation():
     calls.clear()
     ids2 = eng._allocate_writeback_blocks(4, 20)
     assert calls == [] and len(ids2) == 20 and pool.n_free == 17
+
+
+def test_budget_rule_matches_the_reference_table():
+    """SelectedWritebackOps._selection_budget_blocks against the table generated
+    from the reference's own KVScheduler._selection_budget_blocks
+    (core/scheduler.py:547-564; tests/golden/budget.json)."""
+    import json
+    from pathlib import Path
+    rows = json.loads((Path(__file__).parent / "golden" / "budget.json").read_text())
+    pool = PagedKVPool(16, 1, 2, 64, torch.bfloat16, device="cpu", n_total=4)
+    for r in rows:
+        eng = SelectionEngine(pool, num_q_heads=8, sink_len=r["sink"], obs_len=r["obs"], retain_ratio=r["ratio"],
+                              retain_budget_tokens=r["budget"])
+        assert eng._selection_budget_blocks(r["L"]) == (r["k"], r["eff"], r["mode"]), r
+
+
+def test_compress_k_blocks_matches_the_oracle():
+    """BlockAlignedSnapKV's k rule (core/compress.py:133-139) on a grid, against the
+    oracle pinned to the reference's compress fixtures."""
+    from oracle import compress as oc
+    from unifiedkv_b200.compress import BlockAlignedSnapKV
+    for N in (0, 1, 5, 16, 511, 2044, 2045):
+        for sink, obs in ((64, 64), (16, 16), (0, 0), (7, 13)):
+            for budget in (0, 100, 2048, 8192):
+                for ratio in (0.01, 0.2, 0.25, 1.0):
+                    c = BlockAlignedSnapKV(16, sink, obs, retain_ratio=ratio, retain_budget_tokens=budget)
+                    k, mode = c._k_blocks(N)
+                    assert k == oc.compress_k_blocks(N, sink, obs, budget, ratio), (N, sink, obs, budget, ratio)
+                    assert mode == c.compression_mode == ("fixed_budget" if budget > 0 else "ratio")

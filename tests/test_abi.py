@@ -108,3 +108,40 @@ print("ok")
     root = Path(__file__).resolve().parents[1]
     r = subprocess.run([sys.executable, "-c", code], cwd=root, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-3000:]
+
+
+def test_decode_shape_errors_in_reference_order():
+    """Every shape check of page16_decode_attention raises the reference's token
+    (core/page16_native.py:101-124), in the reference's order; the checks run
+    before any device work, so CPU tensors reach them here."""
+    import pytest
+    import torch
+    from unifiedkv_b200.page16_native import page16_decode_attention
+
+    def call(q, k, v, bt, lens, n_rep=2):
+        return page16_decode_attention(q, k, v, bt, lens, softmax_scale=0.1, n_rep=n_rep)
+
+    q = torch.zeros(2, 4, 64)
+    kc = torch.zeros(3, 16, 2, 64)
+    bt = torch.zeros(2, 3, dtype=torch.int32)
+    lens = torch.ones(2, dtype=torch.int32)
+    cases = [
+        (lambda: call(q[0], kc, kc, bt, lens), "q_dim_2"),
+        (lambda: call(q, kc[0], kc, bt, lens), "cache_rank"),
+        (lambda: call(q, kc[:, :8], kc[:, :8], bt, lens), "block_size_8"),
+        (lambda: call(q, kc, kc, bt[0], lens), "block_table_rank"),
+        (lambda: call(q[:0], kc, kc, bt[:0], lens[:0]), "empty"),
+        (lambda: call(q, kc, kc[:, :, :1], bt, lens), "v_cache"),
+        (lambda: call(torch.zeros(2, 3, 64), kc, kc, bt, lens), "gqa"),
+        (lambda: call(q, kc, kc, bt[:1], lens), "block_table_batch"),
+        (lambda: call(q, kc, kc, bt, lens[:1]), "seqlens"),
+        (lambda: call(torch.zeros(2, 4, 512), torch.zeros(3, 16, 2, 512), torch.zeros(3, 16, 2, 512), bt, lens),
+         "head_dim_512"),
+        (lambda: call(q, kc, kc, bt, lens, n_rep=1), "gqa"),  # n_rep disagreeing with the head counts
+    ]
+    for fn, token in cases:
+        with pytest.raises(RuntimeError, match=f"^page16_native_shape_unsupported:{token}$"):
+            fn()
+    # valid shapes on host tensors: refused before any launch
+    with pytest.raises(RuntimeError, match="^page16_native_unavailable:tensors_not_on_cuda$"):
+        call(q, kc, kc, bt, lens)

@@ -51,3 +51,11 @@ def test_token_writes_and_page_reads():
     assert torch.count_nonzero(pool.k_cache[0]) == 0  # the other layer is untouched
     k, v = pool.read_kv_from_blocks(1, [], 5)
     assert k.shape == (2, 0, 8) and v.shape == (2, 0, 8)
+
+
+def test_build_cu_seqlens():
+    """core/varlen.py:12-16: int32 [0, l0, l0+l1, ...]; zero-length sequences keep their slot."""
+    from unifiedkv_b200.varlen import build_cu_seqlens
+    cu = build_cu_seqlens([3, 0, 5, 1], "cpu")
+    assert cu.dtype == torch.int32 and cu.tolist() == [0, 3, 3, 8, 9]
+    assert build_cu_seqlens([], "cpu").tolist() == [0]

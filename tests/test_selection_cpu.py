@@ -93,3 +93,19 @@ def test_compress_k_blocks_matches_the_oracle():
                     k, mode = c._k_blocks(N)
                     assert k == oc.compress_k_blocks(N, sink, obs, budget, ratio), (N, sink, obs, budget, ratio)
                     assert mode == c.compression_mode == ("fixed_budget" if budget > 0 else "ratio")
+
+
+def test_block_indexed_writeback_declines_like_the_reference():
+    """_write_block_indexed_layer_to_pool (core/scheduler.py:702-733) returns False,
+    writing nothing, when the aligned fast path does not apply: no sources, a
+    source/page count mismatch, a length that is not whole pages, a source block
+    out of range."""
+    eng = _engine()
+    K = torch.zeros(2, 64, 64)
+    before = eng.pool.k_cache.clone()
+    assert not eng._write_block_indexed_layer_to_pool(0, [1, 2], K, K, [])
+    assert not eng._write_block_indexed_layer_to_pool(0, [1, 2], K, K, [0])
+    assert not eng._write_block_indexed_layer_to_pool(0, [1], K[:, :60], K[:, :60], [0])
+    assert not eng._write_block_indexed_layer_to_pool(0, [1], K, K, [4])
+    assert not eng._write_block_indexed_layer_to_pool(0, [1, 2], K, K, [-1, 3])
+    assert torch.equal(eng.pool.k_cache, before)

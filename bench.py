@@ -589,7 +589,7 @@ def run_longseq(args, rank, world, local_rank):
         "higher_is_better": True, "scaling": "strong", "dtype": "bf16", "data": "synthetic N(0,1) K/V",
         "config": {"workload": "B=1, 131072 tokens (8192 pages) split over GPUs, 32 layers, 32q/8kv, d128",
                    "parallelism": f"split-KV x{world}" + ("" if world == 1 else (
-                       " + (out, lse) stored into peers' buffers over NVLink, flag-synchronised merge kernel"
+                       " + (out, lse) stored into peers' buffers over NVLink as words carrying the call number, merged in the same kernel"
                        if peer is not None else " + NCCL all-gather of (out, lse)")),
                    "launch": "CUDA graph of the 32-layer step" if graph is not None else "eager"},
         "ms_per_layer": round(ms / layers, 4), "tokens_per_s": round(1000.0 / ms, 2),

@@ -14,12 +14,13 @@ B200 design: one process per GPU (``torch.distributed``, NCCL over NVLink).
     ``lse_out``, and the ranks exchange the [rows, d] partials plus [rows] lse
     and merge them by log-sum-exp.  ``PeerMerge`` does the exchange over NVLink
     peer memory in one kernel (each rank stores its partial straight into every
-    other rank's buffer and raises a flag there, then waits for the other ranks'
-    flags and merges; no collective); without it one NCCL all-gather of packed
-    partials feeds the merge kernel.
-The constructor arguments and the watermark / release methods of the
-reference coordinator are kept; KV-head sharding is not (Page16 needs all
-heads of a page on one GPU).
+    other rank's buffer as 16-byte words that carry the call number, then polls
+    the words the other ranks stored into its own buffer and merges; no fence,
+    flag or collective); without it one NCCL all-gather of packed partials
+    feeds the merge kernel.
+The constructor arguments and the calls of the reference coordinator are kept
+(register, append, evict, watermark, release); KV-head sharding is not (Page16
+needs all heads of a page on one GPU), so a request lives whole on its owner rank.
 """
 from __future__ import annotations
 

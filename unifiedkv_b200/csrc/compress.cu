@@ -19,6 +19,14 @@
 // Every reduction has a fixed order, so the scores are bit-reproducible run to
 // run.  K is read twice (once per pass) straight from HBM in 16-byte cp.async
 // copies; Q of a KV group stays in shared memory for the CTA's token chunk.
+// For head_dim 128 (bf16 / fp16, window rows of a KV group within the tcgen05
+// kernel's limit) both passes run instead as the tcgen05 kernels of
+// compress_tc.cu, whose pass 2 merges the per-range row statistics itself (no
+// reduce launch); the mma.sync kernels here serve the other shapes.  On the
+// tcgen05 path every launch of a compression step (both passes, the block
+// reduction, the top-k, the compaction) is a programmatic dependent launch of
+// the one before it (launch_pdl), each kernel waiting for its predecessor
+// first; the top-k and the compaction are launched that way on both paths.
 #include <type_traits>
 
 #include "common.cuh"

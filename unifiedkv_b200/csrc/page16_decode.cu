@@ -20,7 +20,17 @@
 //    O += P V run on mma.m16n8k16 (fp32 accumulate) with the n_rep heads as
 //    the M rows; P is reused straight from the S accumulators as the A
 //    fragment.  Online softmax in the exp2 domain, row max / sum by quad
-//    shuffles.
+//    shuffles.  bf16 / fp16 P is split into a high and a low part (two MMAs),
+//    keeping about 16 mantissa bits of each weight.
+//  * Launches.  The combine is a programmatic dependent launch of the decode
+//    grid: it is scheduled during the decode grid's tail (the decode CTAs
+//    signal griddepcontrol.launch_dependents once their work is done) and
+//    waits for the grid's completion before reading the partials.  It signals
+//    its own dependents at its start, so a programmatic dependent of the
+//    combine (the NVLink merge of a split sequence) can become resident early.
+//  * Fused append (optional).  With k_new / v_new the warp that owns a
+//    request's last page stores this step's token into the pool and takes its
+//    row from k_new / v_new for the math, so append + decode is one launch.
 #include <mutex>
 #include <type_traits>
 

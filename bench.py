@@ -40,6 +40,11 @@ WORKLOAD = ("llama3.1-8b-shaped page16 decode: 32 layers, 32q/8kv heads, d128, 3
             "ctx U[4096,32768], 16-token pages in a pool of 90% HBM, random block tables")
 
 
+# ncu capture of one decode launch of the --profile-small case: DRAM bytes read + written,
+# and that launch's algorithmic bytes; traffic scales with the bytes a launch must move.
+DECODE_TRAFFIC_PER_ALG_BYTE = (2259438000 + 5422080) / 2259258168
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -345,7 +350,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     launch_gbs = bytes_layer / (launch_ms * 1e-3) / 1e9  # one launch, one GPU
     tokens_per_s = world * BATCH / (ms_per_step * 1e-3)
     if rank != 0:
-        return
+        return None
     line = {
         "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
@@ -360,9 +365,10 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         "hbm_frac_of_measured": round(gbs / world / peak, 4),
         "roofline": {"bound": "hbm", "achieved": round(launch_gbs, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(launch_gbs / peak, 4),
-                     # dram__bytes_read.sum + dram__bytes_write.sum of one decode launch of this
-                     # workload (ncu capture in profiles/page16_decode_llama8b_config2.md)
-                     "traffic": 2259438000 + 5422080,
+                     "traffic": int(round(bytes_layer * DECODE_TRAFFIC_PER_ALG_BYTE)),
+                     "traffic_source": "dram__bytes_read.sum + dram__bytes_write.sum of one decode launch of the "
+                                       "--profile-small case (same per-launch work), per algorithmic byte, "
+                                       "times this launch's algorithmic bytes",
                      "algorithmic_bytes_per_launch": int(bytes_layer),
                      "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                      "kernel": "page16_decode_mma_kernel<bf16,128,8,3> + combine, per layer launch",
@@ -378,7 +384,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         line["config"]["workload"] += " [profiling case: 1 layer, compact pool]"
     if world == 1 and not args.no_cpu_baseline and not args.profile_small:
         line["cpu_baseline"] = cpu_baseline_block(cpu_sample())
-    print(json.dumps(line), flush=True)
+    return line
 
 
 
@@ -442,20 +448,50 @@ def run_prefill(args):
     flops_layer = 4.0 * HQ * D * float(np.sum(chunk * (past + (chunk + 1) / 2.0)))
     tflops = flops_layer * layers / (ms * 1e-3) / 1e12
     hbm, tf, kind = _peaks()
-    print(json.dumps({
+    res = {
         "metric": "paged chunked-prefill attention TFLOP/s (config 5 prefill part)", "value": round(tflops, 2),
         "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "ms_per_layer": round(ms / layers, 5), "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "8 requests x 512-token causal chunks over paged past (lognormal(ln 4000,0.8) "
-                               "clipped [256,32768]), 32 layers, 32q/8kv heads, d128", "past": past.tolist()},
+                               "clipped [256,32768]), 32 layers, 32q/8kv heads, d128", "past": past.tolist(),
+                   "layers": layers},
         "tokens_per_s": round(nreq * chunk / (ms * 1e-3), 1),
         "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": tf, "unit": "TFLOP/s",
                      "frac": round(tflops / tf, 4), "peak_source": f"{kind} bf16_tflops (burst)",
                      "kernel": "prefill_tc_kernel<bf16,paged> (tcgen05, TMEM)",
-                     "note": "algorithmic FLOPs 4*h_q*d*sum(n_q*(past+(n_q+1)/2)); bf16 P is split hi+lo so the "
-                             "tensor pipe executes 1.5x these FLOPs"},
+                     "note": "algorithmic FLOPs 4*h_q*d*sum(n_q*(past+(n_q+1)/2)) (QK^T and PV, causal half of "
+                             "the chunk)" + PREFILL_P_NOTE},
         "gpu_launches": layers * args.steps,
-    }), flush=True)
+    }
+    if not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_prefill_baseline(past, chunk)
+    return res
+
+
+PREFILL_P_NOTE = ""
+
+
+def cpu_prefill_baseline(past, chunk):
+    """The causal chunk-attention restatement (oracle/prefill.py, fp32 numpy, BLAS on every
+    host core) on one layer of the same 8 chunks (K/V of past + chunk per request)."""
+    from oracle.prefill import chunk_attention
+    rng = np.random.default_rng(5)
+    t_total, flops = 0.0, 0.0
+    for p in past:
+        nk = int(p) + chunk
+        q = rng.standard_normal((chunk, HQ, D), dtype=np.float32) * 0.5
+        k = rng.standard_normal((nk, HKV, D), dtype=np.float32) * 0.5
+        v = rng.standard_normal((nk, HKV, D), dtype=np.float32) * 0.5
+        t0 = time.perf_counter()
+        chunk_attention(q, k, v, causal=True, dtype=np.float32)
+        t_total += time.perf_counter() - t0
+        flops += 4.0 * HQ * D * chunk * (int(p) + (chunk + 1) / 2.0)
+    return {"value": round(flops / t_total / 1e12, 5), "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
+            "sample": f"1 of 32 layers x all 8 chunks, fp32 numpy causal chunk attention ({t_total:.2f} s)"}
+
+
+def run_prefill_line(args):
+    print(json.dumps(run_prefill(args)), flush=True)
 
 
 def run_compress(args):
@@ -497,104 +533,237 @@ def run_compress(args):
     bytes_layer = kmid + tq.numel() * 2 + 2 * 2 * eff * 8 * 128 * 2  # K_mid once, Q, retained K+V read+write
     flops_layer = 2 * 2.0 * 32 * 64 * (N * 16) * 128  # QK^T, two passes
     gbs = bytes_layer * layers / (ms * 1e-3) / 1e9
+    tflops = flops_layer * layers / (ms * 1e-3) / 1e12
     hbm, tf, kind = _peaks()
-    print(json.dumps({
-        "metric": "block scoring + top-k + compacting writeback (config 4)", "value": round(ms / layers * 1e3, 2),
+    us_layer = ms / layers * 1e3
+    res = {
+        "metric": "block scoring + top-k + compacting writeback (config 4)", "value": round(us_layer, 2),
         "unit": "us per layer", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": False, "dtype": "bf16", "data": "synthetic (32 hot blocks at +2 sigma)",
         "config": {"workload": "L=32768, 8 kv heads, d128, window 64 x 32 q-heads, keep 25% mid + 4 sink + 8 obs "
-                               "blocks, 32 layers", "k_blocks": k, "effective_len": eff,
+                               "blocks, 32 layers", "k_blocks": k, "effective_len": eff, "layers": layers,
                    "selection": "per_kv_head" if per_head else "shared across kv heads (reference)"},
         "algorithmic_gbs": round(gbs, 1), "hbm_frac_of_measured": round(gbs / hbm, 4),
-        "tflops": round(flops_layer * layers / (ms * 1e-3) / 1e12, 2),
+        "tflops": round(tflops, 2), "tensor_frac_of_measured_burst": round(tflops / tf, 4),
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / hbm, 4), "peak_source": f"{kind} hbm_gbs",
+                     "algorithmic_bytes_per_layer": int(bytes_layer),
+                     "note": "algorithmic bytes = K_mid read once + Q + retained K/V read and written; the score "
+                             f"passes also run 2 x 2*h_q*W*T*d = {flops_layer / 1e9:.1f} GFLOP/layer "
+                             f"({tflops / tf:.3f} of measured bf16 burst)"},
         "gpu_launches": 5 * layers * args.steps,  # score pass 1, pass 2, block reduce, top-k, compaction
-    }), flush=True)
+    }
+    if not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_compress_baseline(K, V, Q, sink, obs, k)
+    return res
 
 
-def run_longseq(args, rank, world, local_rank):
-    """Config 3: one sequence of 131072 tokens (8192 pages), 32 layers; at N>1 the
-    page list is split across GPUs and (out, lse) partials merged over NCCL."""
+def cpu_compress_baseline(K, V, Q, sink, obs, k):
+    """The compression restatement (oracle/compress.py: block scores, lowest-index top-k,
+    writeback gather; pinned to the reference's BlockAlignedSnapKV.compress) on one layer,
+    fp32 numpy on every host core."""
+    from oracle.compress import block_scores, topk_lowest_index, writeback_source_tokens
+    K32, V32, Q32 = (np.asarray(x, np.float32) for x in (K, V, Q))
+    t0 = time.perf_counter()
+    sc = block_scores(K32, Q32, sink, obs, dtype=np.float32)
+    sel = topk_lowest_index(sc, k)
+    src = writeback_source_tokens(K32.shape[1], sink, obs, sel)
+    idx = np.maximum(src, 0)
+    Kf = np.where(src[None, :, None] >= 0, K32[:, idx, :], 0)
+    Vf = np.where(src[None, :, None] >= 0, V32[:, idx, :], 0)
+    dt = time.perf_counter() - t0
+    del Kf, Vf
+    return {"value": round(dt * 1e6, 1), "unit": "us per layer", "cores": cpu_cores(), "kind": "port",
+            "sample": "1 layer of the same input (L=32768, 8 kv heads, 64-query window), fp32 numpy restatement of "
+                      "BlockAlignedSnapKV.compress (core/compress.py:64-175)"}
+
+
+def run_compress_line(args):
+    print(json.dumps(run_compress(args)), flush=True)
+
+
+def _rope(x: "torch.Tensor", positions: "torch.Tensor", theta: float = 500000.0):
+    """Rotary embedding (rotate-half form, Llama) of x [n, ..., d] at positions [n], fp32."""
+    import torch
+    d = x.shape[-1]
+    inv = 1.0 / (theta ** (torch.arange(0, d, 2, device=x.device, dtype=torch.float64) / d))
+    ang = (positions.to(torch.float64)[:, None] * inv[None]).float()  # [n, d/2]
+    shape = [x.shape[0]] + [1] * (x.dim() - 2) + [d // 2]
+    cos, sin = ang.cos().view(shape), ang.sin().view(shape)
+    x1, x2 = x[..., : d // 2], x[..., d // 2:]
+    return torch.cat([x1 * cos - x2 * sin, x1 * sin + x2 * cos], dim=-1)
+
+
+LONGSEQ_TOKENS, LONGSEQ_PAGES = 131072, 8192
+
+
+def longseq_range(layer: int, start: int, end: int, dev):
+    """K/V pages [start, end) of config 3's sequence for one layer: N(0,1), K with RoPE
+    (theta 500000) at its absolute positions, bf16.  Seeded by (layer, start page), so any
+    rank can regenerate another rank's range."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(7_000_003 * (layer + 1) + start)
+    n = end - start
+    k = torch.randn((n * 16, HKV, D), generator=g, device=dev)
+    pos = torch.arange(start * 16, end * 16, device=dev)
+    k = _rope(k, pos).to(torch.bfloat16).view(n, 16, HKV, D)
+    v = torch.randn((n, 16, HKV, D), generator=g, device=dev).to(torch.bfloat16)
+    return k, v
+
+
+def longseq_query(layer: int, dev):
+    import torch
+    g = torch.Generator(device=dev).manual_seed(911 + layer)
+    q = torch.randn((1, HQ, D), generator=g, device=dev)
+    return _rope(q, torch.tensor([LONGSEQ_TOKENS - 1], device=dev)).to(torch.bfloat16)
+
+
+def _reference_fp64(q, k, v, scale):
+    """Plain torch fp64 softmax attention of one query row set over a whole sequence
+    (q [1, h_q, d]; k, v [T, h_kv, d]) on the GPU: the single-GPU check of the split."""
+    import torch
+    rep = HQ // HKV
+    out = torch.empty((HQ, D), dtype=torch.float64, device=q.device)
+    for h in range(HKV):
+        kh = k[:, h].double()
+        vh = v[:, h].double()
+        qh = q[0, h * rep:(h + 1) * rep].double()
+        s = (qh @ kh.T) * scale
+        out[h * rep:(h + 1) * rep] = torch.softmax(s, dim=-1) @ vh
+    return out
+
+
+def run_split_kv(args, rank, world, local_rank, layers=None):
+    """Config 3: one 131072-token sequence (8192 pages), 32 layers, split-KV over the
+    ranks (contiguous page ranges).  N > 1: each layer is bpkv_split_kv_decode_p2p (decode
+    into fp32 CTA partials, then one kernel that combines them, stores the rank's (o, lse)
+    into the peers' buffers over NVLink and merges); N = 1: the plain Page16 decode.  The
+    32-layer step is one CUDA graph.  Layer 0 is checked on rank 0 against a torch fp64
+    attention over the whole sequence, regenerated from the seeds of every rank's range."""
     import torch
     import torch.distributed as dist
-    from unifiedkv_b200.multi_gpu import local_range_lens, split_kv_decode, split_pages
+    from unifiedkv_b200.multi_gpu import PeerMerge, _split_decode, local_range_lens, split_kv_decode, split_pages
+    from unifiedkv_b200.page16_native import page16_decode_attention
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    L, pages = 131072, 8192
-    s, e = split_pages(pages, world)[rank]
-    n_local = e - s
-    layers = 1 if getattr(args, "profile_small", False) else LAYERS
-    g = torch.Generator(device=dev).manual_seed(300 + rank)
-    kp = torch.empty((layers, n_local, 16, HKV, D), dtype=torch.bfloat16, device=dev).normal_(0, 1, generator=g)
-    vp = torch.empty_like(kp).normal_(0, 1, generator=g)
-    gq = torch.Generator(device=dev).manual_seed(299)
-    qs = [(torch.randn(1, HQ, D, device=dev, generator=gq) * 0.5).to(torch.bfloat16) for _ in range(layers)]
-    bt = torch.randperm(n_local, device=dev, generator=g).to(torch.int32)[None]
-    lens = torch.tensor([local_range_lens(L, s, e)], dtype=torch.int32, device=dev)
-    from unifiedkv_b200.page16_native import page16_decode_attention
-
+    layers = layers or (1 if args.profile_small else LAYERS)
+    ranges = split_pages(LONGSEQ_PAGES, world)
+    s, e = ranges[rank]
+    kv = [longseq_range(l, s, e, dev) for l in range(layers)]
+    qs = [longseq_query(l, dev) for l in range(layers)]
+    bt = torch.arange(e - s, dtype=torch.int32, device=dev)[None]
+    lens = torch.tensor([local_range_lens(LONGSEQ_TOKENS, s, e)], dtype=torch.int32, device=dev)
+    scale = D ** -0.5
     exchange = getattr(args, "exchange", "p2p")
-    peer = None
-    if world > 1 and exchange == "p2p":
-        from unifiedkv_b200.multi_gpu import PeerMerge
-        peer = PeerMerge(rows=HQ, head_dim=D, device=dev)
+    peer = PeerMerge(rows=HQ, head_dim=D, device=dev) if world > 1 and exchange == "p2p" else None
+    splits = int(getattr(args, "splits", 0))
+    outs = [None] * layers
+
+    def layer_call(l):
+        k, v = kv[l]
+        if world > 1:
+            return split_kv_decode(qs[l], k, v, bt, lens, scale, HQ // HKV, peer=peer, num_splits=splits)
+        return page16_decode_attention(qs[l], k, v, bt, lens, softmax_scale=scale, n_rep=HQ // HKV)
 
     def step():
         for l in range(layers):
-            if world > 1:
-                split_kv_decode(qs[l], kp[l], vp[l], bt, lens, D ** -0.5, HQ // HKV, peer=peer)
-            else:
-                page16_decode_attention(qs[l], kp[l], vp[l], bt, lens, softmax_scale=D ** -0.5, n_rep=HQ // HKV)
-    for _ in range(args.warmup):
+            outs[l] = layer_call(l)
+
+    def local_only():  # this rank's share without any exchange (the decode + fp32 combine)
+        for l in range(layers):
+            k, v = kv[l]
+            _split_decode(qs[l], k, v, bt, lens, scale, HQ // HKV, out_dtype=torch.bfloat16, num_splits=splits)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def graph_of(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        return g
+
+    for _ in range(max(1, args.warmup)):
         step()
     torch.cuda.synchronize()
-    # the 32-layer step (decode, exchange, merge) is captured once in a CUDA graph:
-    # per-layer work is ~10-90 us, comparable to the Python launch cost
-    graph = None
-    try:
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        graph.replay()
-        torch.cuda.synchronize()
-    except Exception as exc:  # pragma: no cover - capture unsupported: time eager launches
-        graph = None
-        print(f"[bench] CUDA graph capture failed ({exc}); timing eager launches", file=sys.stderr)
-        torch.cuda.synchronize()
-    run = graph.replay if graph is not None else step
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        run()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
     if peer is not None:
         peer.check()
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    # correctness of layer 0 (eager result of the last warm-up step)
+    err = None
+    if rank == 0:
+        ks, vs = zip(*[longseq_range(0, a, b, dev) for a, b in ranges])
+        kfull, vfull = torch.cat(ks).view(-1, HKV, D), torch.cat(vs).view(-1, HKV, D)
+        ref = _reference_fp64(qs[0], kfull, vfull, scale)
+        err = float((outs[0].double().reshape(HQ, D) - ref).abs().max().item())
+        del ks, vs, kfull, vfull, ref
+    barrier()
+    graph = graph_of(step)
+    graph_local = graph_of(local_only) if world > 1 else None
+    torch.cuda.synchronize()
+
+    def timed(g, steps):
+        for _ in range(max(3, args.warmup)):
+            g.replay()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / steps)
+
+    steps = max(3, args.steps)
+    ms = timed(graph, steps)
+    ms_local = timed(graph_local, steps) if graph_local is not None else None
     if peer is not None:
+        peer.check()
         peer.close()  # collective; the captured graph is not replayed after this
     if rank != 0:
-        return
-    bytes_step = L * KV_BYTES_PER_TOKEN * layers
+        return None
+    bytes_step = LONGSEQ_TOKENS * KV_BYTES_PER_TOKEN * layers
     gbs = bytes_step / (ms * 1e-3) / 1e9
-    hbm, tf, kind = _peaks()
-    print(json.dumps({
+    hbm, _, _ = _peaks()
+    res = {
         "metric": "single-sequence 131072-token decode KV-read GB/s (config 3)", "value": round(gbs, 1),
-        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "strong", "dtype": "bf16", "data": "synthetic N(0,1) K/V",
+        "unit": "GB/s", "gb_s": round(gbs, 1), "n_gpus": world, "steps": steps, "ms_per_step": round(ms, 4),
+        "ms_per_layer": round(ms / layers, 5), "tokens_per_s": round(1000.0 / ms, 2),
+        "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+        "data": "synthetic N(0,1) K/V, K with RoPE (theta 500000) at positions 0..131071, q RoPE'd at 131071",
+        "max_abs_err": err,
+        "check": "layer 0 vs torch fp64 attention over the whole sequence on rank 0 (bar 2e-3)",
         "config": {"workload": "B=1, 131072 tokens (8192 pages) split over GPUs, 32 layers, 32q/8kv, d128",
+                   "layers": layers, "pages_per_rank": e - s, "num_splits": splits or "one CTA per SM",
                    "parallelism": f"split-KV x{world}" + ("" if world == 1 else (
-                       " + (out, lse) stored into peers' buffers over NVLink as words carrying the call number, merged in the same kernel"
-                       if peer is not None else " + NCCL all-gather of (out, lse)")),
-                   "launch": "CUDA graph of the 32-layer step" if graph is not None else "eager"},
-        "ms_per_layer": round(ms / layers, 4), "tokens_per_s": round(1000.0 / ms, 2),
+                       ": decode into fp32 CTA partials + one kernel that combines them, exchanges (o, lse) over "
+                       "NVLink peer memory and merges" if peer is not None else
+                       ": fp32 partials + NCCL all-gather + merge kernel")),
+                   "launch": "CUDA graph of the 32-layer step"},
         "hbm_frac_of_measured_per_gpu": round(gbs / world / hbm, 4),
-    }), flush=True)
+        "roofline": {"bound": "hbm", "achieved": round(gbs / world, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(gbs / world / hbm, 4), "per": "GPU (the step reads 512 MiB/N per GPU per layer)"},
+        "gpu_launches": 2 * layers * steps,
+    }
+    if ms_local is not None:
+        res["ms_per_layer_local_decode"] = round(ms_local / layers, 5)
+        res["ms_per_layer_exchange"] = round((ms - ms_local) / layers, 5)
+    return res
+
+
+def run_longseq(args, rank, world, local_rank):
+    res = run_split_kv(args, rank, world, local_rank)
+    if res is not None:
+        print(json.dumps(res), flush=True)
 
 
 def run_mixed(args):
@@ -692,7 +861,13 @@ def run_mixed(args):
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
     toks = n_dec + n_pf * chunk
-    print(json.dumps({
+    # ideal step time: decode KV bytes at the HBM peak + prefill FLOPs at the bf16 peak (+ the
+    # H2D prefetch, which overlaps on the side stream and is not counted)
+    hbm, tf, kind = _peaks()
+    dec_bytes = float(np.sum([lens[sid] for sid in active])) * KV_BYTES_PER_TOKEN * layers
+    pf_flops = 4.0 * HQ * D * float(np.sum(chunk * (pf_past + (chunk + 1) / 2.0))) * layers
+    ideal_ms = (dec_bytes / (hbm * 1e9) + pf_flops / (tf * 1e12)) * 1e3
+    res = {
         "metric": "mixed continuous-batching step tokens/s (config 5)", "value": round(toks / (ms * 1e-3), 1),
         "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
         "higher_is_better": True, "dtype": "bf16", "data": "synthetic (seeded lengths, N(0,0.5) K/V)",
@@ -702,8 +877,91 @@ def run_mixed(args):
                                "inside the decode launch", "layers": layers, "cold_requests": len(cold_len),
                    "decode_ctx_mean": float(np.mean(dec_len)), "prefill_past_mean": float(np.mean(pf_past))},
         "h2d_gb_per_step": round(h2d["bytes"] / args.steps / 1e9, 3),
+        "roofline": {"bound": "hbm+tensor", "achieved": round(ideal_ms / ms, 4), "peak": 1.0, "unit": "fraction",
+                     "frac": round(ideal_ms / ms, 4), "ideal_ms_per_step": round(ideal_ms, 3),
+                     "note": "ideal = decode KV bytes / measured HBM peak + prefill FLOPs / measured bf16 burst; "
+                             "frac = ideal / measured step time"},
+        "gpu_launches": 2 * layers * args.steps,
         "offload_stats": mgr.get_stats(),
-    }), flush=True)
+    }
+    if not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_mixed_baseline(dec_len, pf_past, chunk)
+    return res
+
+
+def cpu_mixed_baseline(dec_len, pf_past, chunk, n_dec_sample=8):
+    """One layer of the mixed step on the host cores (fp32 numpy restatements): decode of
+    8 of the 56 requests (oracle/page16.py) and one 512-token chunk (oracle/prefill.py),
+    extrapolated to the whole 32-layer step (56 decode + 8 chunks)."""
+    from oracle.page16 import page16_decode_reference
+    from oracle.prefill import chunk_attention
+    rng = np.random.default_rng(6)
+    lens = np.asarray(dec_len[:n_dec_sample], np.int32)
+    need = (lens + 15) // 16
+    k = rng.standard_normal((int(need.sum()), 16, HKV, D), dtype=np.float32) * 0.5
+    v = rng.standard_normal(k.shape, dtype=np.float32) * 0.5
+    q = rng.standard_normal((len(lens), HQ, D), dtype=np.float32) * 0.5
+    bt = np.zeros((len(lens), int(need.max())), np.int32)
+    off = 0
+    for b, n in enumerate(need):
+        bt[b, :n] = np.arange(off, off + n)
+        off += int(n)
+    t0 = time.perf_counter()
+    page16_decode_reference(q, k, v, bt, lens, D ** -0.5, HQ // HKV, compute_dtype=np.float32)
+    t_dec = time.perf_counter() - t0
+    nk = int(pf_past[0]) + chunk
+    qc = rng.standard_normal((chunk, HQ, D), dtype=np.float32) * 0.5
+    kc = rng.standard_normal((nk, HKV, D), dtype=np.float32) * 0.5
+    vc = rng.standard_normal((nk, HKV, D), dtype=np.float32) * 0.5
+    t0 = time.perf_counter()
+    chunk_attention(qc, kc, vc, causal=True, dtype=np.float32)
+    t_pf = time.perf_counter() - t0
+    # scale the samples to the full step: decode by context tokens, prefill by chunk FLOPs
+    dec_scale = float(np.sum(dec_len)) / float(np.sum(lens))
+    pf_scale = float(np.sum(pf_past + (chunk + 1) / 2.0)) / float(pf_past[0] + (chunk + 1) / 2.0)
+    step_s = LAYERS * (t_dec * dec_scale + t_pf * pf_scale)
+    toks = len(dec_len) + len(pf_past) * chunk
+    return {"value": round(toks / step_s, 3), "unit": "tokens/s", "cores": cpu_cores(), "kind": "port",
+            "sample": f"1 layer: decode of {len(lens)} of {len(dec_len)} requests ({t_dec:.2f} s) + 1 of "
+                      f"{len(pf_past)} chunks ({t_pf:.2f} s), fp32 numpy, extrapolated to 32 layers x the whole batch"}
+
+
+def run_mixed_line(args):
+    print(json.dumps(run_mixed(args)), flush=True)
+
+
+def _free_cuda():
+    import gc
+    import torch
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+
+def run_default(args, rank, world, local_rank):
+    """The driver's run: the headline decode line, with config 3 (split-KV, every N) and,
+    at N = 1, configs 4 and 5 attached as extra keys, each measured after the previous
+    workload's memory is released."""
+    line = run_ours(args, rank, world, local_rank)
+    if args.no_extras or args.profile_small:
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    _free_cuda()
+    extra = argparse.Namespace(**vars(args))
+    extra.steps, extra.warmup = max(3, min(args.steps, 10)), max(3, min(args.warmup, 5))
+    sk = run_split_kv(extra, rank, world, local_rank)
+    _free_cuda()
+    if rank == 0:
+        line["split_kv"] = sk
+        if world == 1:
+            for key, fn in (("compress", run_compress), ("prefill", run_prefill), ("mixed", run_mixed)):
+                line[key] = fn(extra)
+                _free_cuda()
+            line["gpu_launches_extras"] = {k: line[k]["gpu_launches"] for k in ("split_kv", "compress", "prefill",
+                                                                               "mixed")}
+        print(json.dumps(line), flush=True)
+
 
 def main():
     ap = argparse.ArgumentParser()
@@ -718,6 +976,10 @@ def main():
                     help="longseq workload at N>1: partial exchange over NVLink peer memory or NCCL all-gather")
     ap.add_argument("--per-kv-head", action="store_true",
                     help="compress workload: per-KV-head block selection instead of the shared one")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="decode workload: print the headline line only (no config 3/4/5 keys)")
+    ap.add_argument("--splits", type=int, default=0,
+                    help="split-KV workload: decode CTAs over the page list (0 = one per SM)")
     ap.add_argument("--profile-small", action="store_true",
                     help="ncu case: 1 layer, pool of only the needed pages (same per-launch work)")
     args = ap.parse_args()
@@ -734,11 +996,11 @@ def main():
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     try:
         if args.workload == "decode":
-            run_ours(args, rank, world, local_rank)
+            run_default(args, rank, world, local_rank)
         elif args.workload == "longseq":
             run_longseq(args, rank, world, local_rank)
         elif rank == 0:
-            {"prefill": run_prefill, "compress": run_compress, "mixed": run_mixed}[args.workload](args)
+            {"prefill": run_prefill_line, "compress": run_compress_line, "mixed": run_mixed_line}[args.workload](args)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -50,6 +50,11 @@ BPKV_API const char* bpkv_last_error(void);
 /* Library version (major*10000 + minor*100 + patch). */
 BPKV_API int bpkv_version(void);
 
+/* Hash of the sources the library was built from (16 hex digits; build.py's
+ * tree_hash over csrc/*.cu, csrc/*.cuh, include/*.h).  The Python loader refuses
+ * a library whose hash differs from the tree it sits in. */
+BPKV_API const char* bpkv_build_hash(void);
+
 /* Number of streaming multiprocessors of the current device (cached per device). */
 BPKV_API int bpkv_num_sms(void);
 
@@ -161,10 +166,10 @@ BPKV_API int bpkv_lse_combine(const float* part_out, const float* part_lse, void
  * graph and replayed):
  *   bpkv_split_kv_merge_p2p: this rank's partial part_out [rows, head_dim]
  *   (dtype) with natural-log part_lse [rows] is stored into every rank's
- *   buffer over NVLink as 16-byte words that carry the call number beside
- *   each pair of values (no separate flag or fence), then every rank polls
- *   the words of this call and writes the merged out [rows, head_dim] (and
- *   lse_out [rows] if not null).  The launch is a programmatic dependent
+ *   buffer over NVLink as 16-byte words of two 64-bit halves, each an fp32
+ *   value beside the call number (no separate flag or fence), then every rank
+ *   polls the words of this call and writes the merged out [rows, head_dim]
+ *   in out_dtype (and lse_out [rows] if not null).  The launch is a programmatic dependent
  *   launch: it may start during the grid that produced part_out and waits
  *   for it.  A wait gives up after max_polls polls (or 4 s): *status is set
  *   to 1 and the rows are NaN.
@@ -178,7 +183,35 @@ BPKV_API int bpkv_peer_buffer_close(void* ptr);
 BPKV_API int bpkv_peer_buffer_free(void* ptr);
 BPKV_API int bpkv_split_kv_merge_p2p(const void* part_out, const float* part_lse, void* const* peer_bufs,
                      int rank, int world, int rows, int head_dim, uint32_t max_polls,
-                     void* out, float* lse_out, int* status, int dtype, void* stream);
+                     void* out, float* lse_out, int* status, int dtype, int out_dtype, void* stream);
+
+/* ------------------------------------------------------------------------ *
+ * Split-KV decode of sequences whose pages are split across GPUs, with the
+ * exchange fused into the combine.  Replaces, for one long sequence, the
+ * reference's multi-GPU decode (core/multi_gpu.py:7-123 mirrors KV heads and
+ * decode falls back to a dense rebuild, core/engine.py:2841-2851).
+ * Arguments up to workspace_bytes are those of bpkv_page16_decode, for THIS
+ * rank's page range (block table and token counts of the range), except that
+ * out is [batch, num_q_heads, head_dim] in out_dtype (dtype, or BPKV_F32).
+ * Two launches: the decode grid (num_splits CTAs over the flattened page list,
+ * 0 = one per SM) leaves an fp32 partial per CTA; a programmatic dependent
+ * kernel, one CTA per (request, q-head) row, merges the row's partials in fp32,
+ * stores the rank's (o, lse) into every peer's exchange buffer (peer_bufs as
+ * for bpkv_split_kv_merge_p2p, rows = batch * num_q_heads; may be NULL when
+ * world == 1), polls the peers' words of this call and writes the merged row
+ * once (lse_out optional, natural log).  No partial is rounded to a 16-bit
+ * type before the final merge.  Rows with no keys on any rank are NaN (lse
+ * -inf).  A wait gives up after max_polls polls (or 4 s): *status = 1 and the
+ * row is NaN.  world <= 8; head_dim % 4 == 0.  No multicast.
+ * ------------------------------------------------------------------------ */
+BPKV_API int bpkv_split_kv_decode_p2p(const void* q, const void* k_cache, const void* v_cache,
+                     const int32_t* block_table, const int32_t* cache_seqlens, void* out,
+                     float* lse_out, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                     int max_blocks, int64_t q_stride_b, int64_t q_stride_h, int64_t page_stride,
+                     int64_t bt_stride_b, float softmax_scale, int dtype, int out_dtype,
+                     void* workspace, size_t workspace_bytes, int num_splits,
+                     void* const* peer_bufs, int rank, int world, uint32_t max_polls,
+                     int* status, void* stream);
 
 /* ------------------------------------------------------------------------ *
  * Decode-token append: writes this step's k/v into the paged pool at slot

@@ -44,10 +44,23 @@ def test_new_entry_points_validate_without_gpu():
     L = _lib.load()
     assert L.bpkv_peer_exchange_bytes(0, 32, 128) == 0 and L.bpkv_peer_exchange_bytes(9, 32, 128) == 0
     assert L.bpkv_peer_exchange_bytes(2, 32, 128) >= 2 * 2 * 32 * 132 * 4
-    rc = L.bpkv_split_kv_merge_p2p(None, None, None, 3, 2, 32, 128, 100, None, None, None, 2, None)
+    rc = L.bpkv_split_kv_merge_p2p(None, None, None, 3, 2, 32, 128, 100, None, None, None, 2, 2, None)
     assert rc == _lib.BPKV_ERR_SHAPE and "rank_3_of_2" in _lib.last_error()
-    rc = L.bpkv_split_kv_merge_p2p(None, None, None, 0, 2, 32, 126, 100, None, None, None, 2, None)
+    rc = L.bpkv_split_kv_merge_p2p(None, None, None, 0, 2, 32, 126, 100, None, None, None, 2, 2, None)
     assert rc == _lib.BPKV_ERR_SHAPE and "head_dim" in _lib.last_error()
+    # fused split-KV decode: rank / head_dim / out dtype / peer buffers are checked first
+    args = [None] * 7 + [1, 32, 8, 128, 10, 0, 0, 0, 0, 0.1, 2, 2, None, 0, 0]
+    rc = L.bpkv_split_kv_decode_p2p(*args, None, 2, 2, 100, None, None)
+    assert rc == _lib.BPKV_ERR_SHAPE and "rank_2_of_2" in _lib.last_error()
+    dummy = ctypes.c_int(0)
+    rc = L.bpkv_split_kv_decode_p2p(*args, None, 0, 2, 100, ctypes.byref(dummy), None)
+    assert rc == _lib.BPKV_ERR_SHAPE and "null_pointer" in _lib.last_error()
+    bad = list(args)
+    bad[18] = 1  # out_dtype fp16 with bf16 inputs
+    rc = L.bpkv_split_kv_decode_p2p(*bad, None, 0, 1, 100, ctypes.byref(dummy), None)
+    assert rc == _lib.BPKV_ERR_SHAPE and "out_dtype" in _lib.last_error()
+    rc = L.bpkv_split_kv_decode_p2p(*args, None, 0, 1, 100, ctypes.byref(dummy), None)
+    assert rc == _lib.BPKV_ERR_SHAPE and "null_pointer" in _lib.last_error()  # q is NULL
     rc = L.bpkv_topk_select_batched(None, 10, 3, -1, None, None)
     assert rc == _lib.BPKV_ERR_SHAPE
     rc = L.bpkv_page_compact_per_kv_head(None, None, None, None, None, 3, 4, None, 100, 16, 16, 8, 128,

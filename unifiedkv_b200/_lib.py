@@ -29,6 +29,7 @@ _c_u32 = ctypes.c_uint32
 SIGNATURES = {
     "bpkv_last_error": (ctypes.c_char_p, []),
     "bpkv_version": (_c_int, []),
+    "bpkv_build_hash": (ctypes.c_char_p, []),
     "bpkv_num_sms": (_c_int, []),
     "bpkv_page16_decode_workspace_size": (_c_sz, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "bpkv_page16_decode": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
@@ -49,7 +50,11 @@ SIGNATURES = {
     "bpkv_peer_buffer_close": (_c_int, [_c_p]),
     "bpkv_peer_buffer_free": (_c_int, [_c_p]),
     "bpkv_split_kv_merge_p2p": (_c_int, [_c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int, _c_u32, _c_p, _c_p,
-                                         _c_p, _c_int, _c_p]),
+                                         _c_p, _c_int, _c_int, _c_p]),
+    "bpkv_split_kv_decode_p2p": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
+                                          _c_int, _c_int, _c_int, _c_int, _c_int,
+                                          _c_i64, _c_i64, _c_i64, _c_i64, _c_f, _c_int, _c_int,
+                                          _c_p, _c_sz, _c_int, _c_p, _c_int, _c_int, _c_u32, _c_p, _c_p]),
     "bpkv_decode_append": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_int, _c_int, _c_int, _c_int,
                                     _c_i64, _c_i64, _c_i64, _c_int, _c_p]),
     "bpkv_block_score_workspace_size": (_c_sz, [_c_int, _c_int, _c_int, _c_int, _c_int]),
@@ -99,9 +104,27 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
                 continue
             fn.restype = res
             fn.argtypes = args
-        lib.bpkv_missing_symbols = missing
+        if missing:  # a library built from other sources: refuse it now, not at the first call
+            _load_error = f"{p}: missing symbols {missing}"
+            raise RuntimeError(f"page16_native_unavailable:stale_library:missing_{','.join(missing)}")
+        _check_build_hash(lib, p)
         _lib = lib
         return lib
+
+
+def _check_build_hash(lib: ctypes.CDLL, p: Path) -> None:
+    """The library must have been built from the sources beside it (when they are
+    present: the package tree always ships them)."""
+    global _load_error
+    from . import build as _build
+    if not _build.CSRC.is_dir() or not any(_build.CSRC.glob("*.cu")):
+        return
+    want = _build.tree_hash()
+    have = lib.bpkv_build_hash().decode("ascii", "replace")
+    if have != want:
+        _load_error = f"{p}: built from sources {have}, tree is {want}"
+        raise RuntimeError(f"page16_native_unavailable:stale_library:built_{have}_tree_{want}"
+                           " (rebuild with python -m unifiedkv_b200.build)")
 
 
 def available() -> bool:

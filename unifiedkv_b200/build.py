@@ -5,6 +5,7 @@ with the source tree; nothing is installed into site-packages.
 """
 from __future__ import annotations
 
+import hashlib
 import os
 import shutil
 import subprocess
@@ -36,27 +37,51 @@ def sources() -> list[Path]:
     return sorted(CSRC.glob("*.cu"))
 
 
+def tree_hash() -> str:
+    """SHA-256 (first 16 hex digits) over the names and contents of every source
+    the library is built from: csrc/*.cu, csrc/*.cuh, include/*.h."""
+    h = hashlib.sha256()
+    deps = sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h")))
+    for p in deps:
+        h.update(p.name.encode())
+        h.update(b"\0")
+        h.update(p.read_bytes())
+        h.update(b"\0")
+    return h.hexdigest()[:16]
+
+
+def library_hash(lib: Path = LIB) -> str | None:
+    """The tree hash the library at ``lib`` was built from (bpkv_build_hash()),
+    read in a child process so that this process never maps a library that is
+    about to be replaced."""
+    if not lib.exists():
+        return None
+    code = ("import ctypes,sys; L=ctypes.CDLL(sys.argv[1]); f=L.bpkv_build_hash; "
+            "f.restype=ctypes.c_char_p; print(f().decode())")
+    r = subprocess.run([sys.executable, "-c", code, str(lib)], capture_output=True, text=True)
+    return r.stdout.strip() if r.returncode == 0 else None
+
+
 def _stale() -> bool:
-    if not LIB.exists():
-        return True
-    t = LIB.stat().st_mtime
-    deps = list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cuh")) + list(INCLUDE.glob("*.h"))
-    return any(p.stat().st_mtime > t for p in deps)
+    return library_hash() != tree_hash()
 
 
 def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> Path:
-    """Compile every ``csrc/*.cu`` into ``lib/libbpkv.so`` (skips if up to date)."""
+    """Compile every ``csrc/*.cu`` into ``lib/libbpkv.so``.  Skipped only when the
+    existing library reports the hash of the current sources (bpkv_build_hash)."""
     if not force and not _stale():
         return LIB
     LIBDIR.mkdir(parents=True, exist_ok=True)
     objdir = LIBDIR / ("obj_trace" if os.environ.get("BPKV_TRACE") == "1" else "obj")
     objdir.mkdir(exist_ok=True)
     nvcc = _nvcc()
+    stamp = tree_hash()
     objs = []
     procs = []
     for src in sources():
         obj = objdir / (src.stem + ".o")
-        cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
+        cmd = [nvcc, *ARCH, *NVCC_FLAGS, "-I", str(INCLUDE), f"-DBPKV_BUILD_HASH=\"{stamp}\"", "-c", str(src),
+               "-o", str(obj)]
         if os.environ.get("BPKV_TRACE") == "1":  # debug instrumentation build (separate library)
             cmd += ["-DBPKV_TRACE"]
         if ptxas_verbose:

@@ -36,6 +36,12 @@ int sm_count() {
 
 extern "C" BPKV_API const char* bpkv_last_error(void) { return bpkv::g_err; }
 
-extern "C" BPKV_API int bpkv_version(void) { return 100; }
+extern "C" BPKV_API int bpkv_version(void) { return 200; }
+
+#ifndef BPKV_BUILD_HASH
+#define BPKV_BUILD_HASH "unstamped"
+#endif
+// Hash of the sources this library was built from (unifiedkv_b200/build.py, tree_hash).
+extern "C" BPKV_API const char* bpkv_build_hash(void) { return BPKV_BUILD_HASH; }
 
 extern "C" BPKV_API int bpkv_num_sms(void) { return bpkv::sm_count(); }

@@ -34,7 +34,10 @@
 #include <mutex>
 #include <type_traits>
 
+#include <string.h>
+
 #include "common.cuh"
+#include "peer_words.cuh"
 
 namespace bpkv {
 namespace {
@@ -58,6 +61,10 @@ struct DecodeParams {
   const void* k_new;
   const void* v_new;
   int64_t new_sb;
+  // split-KV across GPUs: every CTA writes its fp32 partial to its slot (no direct
+  // T output even for a request a single CTA owns), for the fused exchange kernel
+  int partials_only;
+  int num_splits;  // CTAs over the flattened page list; 0 = one per SM (per KV-head group)
 };
 
 constexpr float kLn2 = 0.6931471805599453f;
@@ -237,7 +244,7 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
     const float inv0 = 1.f / L0, inv1 = 1.f / L1;
     const float lse0 = (m0 + __log2f(L0)) * kLn2;
     const float lse1 = (m1 + __log2f(L1)) * kLn2;
-    const bool whole = seg_first == prefix[b] && seg_end == prefix[b + 1];
+    const bool whole = !p.partials_only && seg_first == prefix[b] && seg_end == prefix[b + 1];
     const int hq0 = h * p.n_rep + row0, hq1 = h * p.n_rep + row1;
     if (whole) {
       T* ob = reinterpret_cast<T*>(p.out) + static_cast<int64_t>(b) * p.Hq * D;
@@ -421,7 +428,7 @@ __global__ void __launch_bounds__(NW * 32) page16_decode_generic_kernel(DecodePa
     int cur_b = -1, cur_len = 0;
     int64_t seg_first = 0;
     auto finish = [&](int b, int64_t seg_end) {
-      const bool whole = seg_first == prefix[b] && seg_end == prefix[b + 1];
+      const bool whole = !p.partials_only && seg_first == prefix[b] && seg_end == prefix[b + 1];
       const float inv = 1.f / l;
       const float lse = m + logf(l);
       if (whole) {
@@ -623,6 +630,191 @@ __global__ void lse_combine_kernel(const float* part_o, const float* part_lse, v
 }
 
 // ---------------------------------------------------------------------------
+// Split-KV decode of sequences whose pages are split across GPUs: the decode
+// grid (partials_only) leaves one fp32 partial per CTA of every request, and
+// this kernel - a programmatic dependent launch of that grid - does the rest of
+// the layer in one pass per row r = (request b, q-head), one CTA of kCombWarps
+// warps per row:
+//   1. local combine: the row's CTA partials (fp32, workspace slots) merged by
+//      log-sum-exp into this rank's (o, lse), kept in shared memory in fp32;
+//   2. exchange: (o, lse) stored into every peer's exchange buffer as words
+//      that carry the call number (peer_words.cuh), over NVLink;
+//   3. merge: the peers' words for this row polled from this rank's own buffer
+//      (bounded waits) and merged with the own (o, lse) in fp32, written once as
+//      T (and lse_out).
+// So no partial is ever rounded to T before the final merge, and a layer is two
+// launches (decode, this) instead of three.  With world == 1 steps 2 and 3 are
+// skipped.  A wait that runs out sets *status = 1 and writes a NaN row.
+// ---------------------------------------------------------------------------
+struct PeerSet {
+  uint4* bufs[peer::kMaxRanks];
+  int* status;
+  int rank, world;
+  uint32_t max_polls;
+};
+
+template <typename T, typename TO>
+__global__ void __launch_bounds__(kCombWarps * 32) split_kv_p2p_kernel(DecodeParams p, int G,
+                                                                       const __grid_constant__ PeerSet ps) {
+  __shared__ int s_slot[kMaxSlotsPerReq];
+  __shared__ float s_w[kMaxSlotsPerReq];
+  __shared__ float s_red[kCombWarps];
+  __shared__ float s_acc[kCombWarps][256];
+  __shared__ float s_o[256];
+  __shared__ float s_lq[peer::kMaxRanks];
+  __shared__ int s_n;
+  pdl_wait();  // the decode grid's partials and prefix are complete and visible
+  const int r = blockIdx.x, rows = p.B * p.Hq;
+  const int b = r / p.Hq, hq = r % p.Hq;
+  const int D = p.D, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t T_ = p.g_prefix[p.B];
+  const int64_t first = p.g_prefix[b], last = p.g_prefix[b + 1];
+  // ---- 1. local combine of the CTA partials of request b ----
+  float M = -INFINITY, W = 0.f;
+  if (last > first) {
+    const int c_lo = owner_of_page(first, T_, G), c_hi = owner_of_page(last - 1, T_, G);
+    const bool dense = T_ >= G;
+    if (!dense && tid == 0) {
+      int n = 0;
+      int64_t start = range_start(c_lo, T_, G);
+      for (int c = c_lo; c <= c_hi && n < kMaxSlotsPerReq; ++c) {
+        const int64_t next = range_start(c + 1, T_, G);
+        if (next > start) s_slot[n++] = c + b;
+        start = next;
+      }
+      s_n = n;
+    }
+    __syncthreads();
+    const int n = dense ? min(c_hi - c_lo + 1, kMaxSlotsPerReq) : s_n;
+    auto slot = [&](int i) { return dense ? (c_lo + i + b) : s_slot[i]; };
+    for (int i = tid; i < n; i += blockDim.x) M = fmaxf(M, p.part_lse[static_cast<int64_t>(slot(i)) * p.Hq + hq]);
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (lane == 0) s_red[warp] = M;
+    __syncthreads();
+    M = s_red[0];
+    for (int w = 1; w < kCombWarps; ++w) M = fmaxf(M, s_red[w]);
+    __syncthreads();
+    for (int i = tid; i < n; i += blockDim.x) {
+      const float wi = expf(p.part_lse[static_cast<int64_t>(slot(i)) * p.Hq + hq] - M);
+      s_w[i] = wi;
+      W += wi;
+    }
+    for (int o = 16; o > 0; o >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o);
+    if (lane == 0) s_red[warp] = W;
+    __syncthreads();
+    W = 0.f;
+    for (int w = 0; w < kCombWarps; ++w) W += s_red[w];
+    float acc[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
+    for (int i = warp; i < n; i += kCombWarps) {
+      const float* po = p.part_o + (static_cast<int64_t>(slot(i)) * p.Hq + hq) * D;
+      const float wi = s_w[i];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int d = lane + 32 * k;
+        if (d < D) acc[k] += wi * po[d];
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int d = lane + 32 * k;
+      if (d < D) s_acc[warp][d] = acc[k];
+    }
+    __syncthreads();
+    const float inv = 1.f / W;
+    for (int d = tid; d < D; d += blockDim.x) {
+      float a = 0.f;
+      for (int w = 0; w < kCombWarps; ++w) a += s_acc[w][d];
+      s_o[d] = a * inv;
+    }
+  } else {
+    for (int d = tid; d < D; d += blockDim.x) s_o[d] = 0.f;
+  }
+  const float lse_mine = (W > 0.f) ? M + logf(W) : -INFINITY;
+  __syncthreads();
+  // ---- 2. exchange ----
+  const int H = D / 2;
+  uint32_t epoch = 0;
+  int par = 0;
+  if (ps.world > 1) {
+    uint4* own = ps.bufs[ps.rank];
+    epoch = *peer::epoch_ptr(own, ps.world, rows, D) + 1u;
+    par = static_cast<int>(epoch & 1u);
+    const int nw = H + 1;
+    for (int e = tid; e < (ps.world - 1) * nw; e += blockDim.x) {
+      const int i = e / nw, j = e % nw;
+      const int pr = (ps.rank + 1 + i) % ps.world;
+      const float x0 = j < H ? s_o[2 * j] : lse_mine;
+      const float x1 = j < H ? s_o[2 * j + 1] : 0.f;
+      peer::st_word(peer::row_ptr(ps.bufs[pr], ps.world, rows, D, par, ps.rank, r) + j, x0, x1, epoch);
+    }
+  }
+  // ---- 3. merge ----
+  const uint64_t t0 = peer::now_ns();
+  uint32_t polls = 0;
+  bool ok = true;
+  if (tid < peer::kMaxRanks) {
+    float lq = -INFINITY;
+    if (tid == ps.rank) {
+      lq = lse_mine;
+    } else if (tid < ps.world) {
+      float unused;
+      ok = peer::wait_word(peer::row_ptr(ps.bufs[ps.rank], ps.world, rows, D, par, tid, r) + H, epoch, polls,
+                           ps.max_polls, t0, lq, unused);
+    }
+    s_lq[tid] = lq;
+  }
+  const bool failed_lse = __syncthreads_or(!ok);
+  float Mg = -INFINITY;
+  for (int q = 0; q < ps.world; ++q) Mg = fmaxf(Mg, s_lq[q]);
+  float wq[peer::kMaxRanks], Wg = 0.f;
+#pragma unroll
+  for (int q = 0; q < peer::kMaxRanks; ++q) {
+    wq[q] = (q < ps.world && Mg != -INFINITY) ? expf(s_lq[q] - Mg) : 0.f;
+    Wg += wq[q];
+  }
+  float v0 = 0.f, v1 = 0.f;
+  if (!failed_lse && Mg != -INFINITY && tid < H) {
+    for (int q = 0; q < ps.world; ++q) {
+      if (!(wq[q] > 0.f)) continue;
+      float x0, x1;
+      if (q == ps.rank) {
+        x0 = s_o[2 * tid];
+        x1 = s_o[2 * tid + 1];
+      } else if (!peer::wait_word(peer::row_ptr(ps.bufs[ps.rank], ps.world, rows, D, par, q, r) + tid, epoch,
+                                  polls, ps.max_polls, t0, x0, x1)) {
+        ok = false;
+        x0 = x1 = 0.f;
+      }
+      v0 += wq[q] * x0;
+      v1 += wq[q] * x1;
+    }
+  }
+  const bool failed = __syncthreads_or(!ok);
+  TO* ob = reinterpret_cast<TO*>(p.out) + static_cast<int64_t>(r) * D;
+  const float nan = __int_as_float(0x7fc00000);
+  if (failed || Mg == -INFINITY) {  // a wait ran out, or no rank had keys for this row (the reference's 0/0)
+    for (int d = tid; d < D; d += blockDim.x) ob[d] = Elem<TO>::from_f(nan);
+    if (tid == 0) {
+      if (p.lse_out != nullptr) p.lse_out[r] = failed ? nan : -INFINITY;
+      if (failed) atomicExch(ps.status, 1);
+    }
+  } else {
+    const float invg = 1.f / Wg;
+    if (tid < H) {
+      ob[2 * tid] = Elem<TO>::from_f(v0 * invg);
+      ob[2 * tid + 1] = Elem<TO>::from_f(v1 * invg);
+    }
+    if (tid == 0 && p.lse_out != nullptr) p.lse_out[r] = Mg + logf(Wg);
+  }
+  if (ps.world > 1) {
+    __syncthreads();
+    if (tid == 0) peer::finish_call(ps.bufs[ps.rank], ps.world, rows, D, epoch);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Decode-token append.
 
 // Append for the generic decode path: the new token goes to position len-1 (lengths include it).
@@ -695,10 +887,18 @@ bool set_smem(K kernel, size_t bytes, bool* done) {
   return true;
 }
 
+// CTAs over the flattened page list: one per SM and KV-head group by default, or the
+// caller's split count (at most 2 per SM: the workspace holds 2*SMs + B partial slots).
+inline int decode_grid(const DecodeParams& p, int groups) {
+  const int dflt = max(1, sm_count() / groups);
+  if (p.num_splits <= 0) return dflt;
+  return max(1, min(p.num_splits, 2 * sm_count() / groups));
+}
+
 template <typename T, int D, int NW, int NS>
-int launch_mma(DecodeParams& p, cudaStream_t st) {
+int launch_mma(DecodeParams& p, cudaStream_t st, bool combine) {
   const int groups = (p.Hkv + NW - 1) / NW;
-  const int G = max(1, sm_count() / groups);
+  const int G = decode_grid(p, groups);
   const size_t smem = static_cast<size_t>(NW) * NS * 2 * 16 * D * 2 + sizeof(int) * (p.B + 1);
   auto kern = page16_decode_mma_kernel<T, D, NW, NS>;
   static bool done[64] = {false};
@@ -707,6 +907,7 @@ int launch_mma(DecodeParams& p, cudaStream_t st) {
     return BPKV_ERR_CUDA;
   }
   kern<<<dim3(G, groups), NW * 32, smem, st>>>(p);
+  if (!combine) BPKV_RETURN_LAUNCH("page16_native_launch");
   // the combine overlaps its launch with the decode grid's tail (programmatic dependent launch)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.B, p.Hq, (p.D + 31) / 32);
@@ -735,10 +936,10 @@ template <typename T>
 __global__ void decode_append_len_kernel(DecodeParams p);
 
 template <typename T>
-int launch_generic(DecodeParams& p, cudaStream_t st) {
+int launch_generic(DecodeParams& p, cudaStream_t st, bool combine) {
   constexpr int NW = 8;
   if (p.k_new != nullptr) decode_append_len_kernel<T><<<p.B, 256, 0, st>>>(p);  // append, then decode
-  const int G = sm_count();
+  const int G = decode_grid(p, 1);
   const size_t smem = sizeof(int) * (p.B + 1);
   auto kern = page16_decode_generic_kernel<T, NW>;
   static bool done[64] = {false};
@@ -747,20 +948,28 @@ int launch_generic(DecodeParams& p, cudaStream_t st) {
     return BPKV_ERR_CUDA;
   }
   kern<<<G, NW * 32, smem, st>>>(p);
+  if (!combine) BPKV_RETURN_LAUNCH("page16_native_launch");
   page16_decode_combine_kernel<T><<<dim3(p.B, p.Hq, (p.D + 31) / 32), kCombWarps * 32, 0, st>>>(p, G);
   BPKV_RETURN_LAUNCH("page16_native_launch");
 }
 
+// Decode grid G of the launch that dispatch() makes for these parameters.
+inline int dispatch_grid(const DecodeParams& p, bool fast_ok) {
+  if (fast_ok && p.D == 256) return decode_grid(p, (p.Hkv + 3) / 4);
+  if (fast_ok) return decode_grid(p, (p.Hkv + 7) / 8);
+  return decode_grid(p, 1);
+}
+
 template <typename T>
-int dispatch(DecodeParams& p, cudaStream_t st, bool fast_ok) {
+int dispatch(DecodeParams& p, cudaStream_t st, bool fast_ok, bool combine = true) {
   if constexpr (!std::is_same<T, float>::value) {
     if (fast_ok) {
-    if (p.D == 128) return launch_mma<T, 128, 8, 3>(p, st);
-    if (p.D == 64) return launch_mma<T, 64, 8, 6>(p, st);
-    if (p.D == 256) return launch_mma<T, 256, 4, 3>(p, st);
+      if (p.D == 128) return launch_mma<T, 128, 8, 3>(p, st, combine);
+      if (p.D == 64) return launch_mma<T, 64, 8, 6>(p, st, combine);
+      if (p.D == 256) return launch_mma<T, 256, 4, 3>(p, st, combine);
     }
   }
-  return launch_generic<T>(p, st);
+  return launch_generic<T>(p, st, combine);
 }
 
 }  // namespace
@@ -776,14 +985,14 @@ extern "C" BPKV_API size_t bpkv_page16_decode_workspace_size(int batch, int num_
   return ws_layout(batch, num_q_heads, head_dim).total;
 }
 
-static int page16_decode_impl(const void* q, const void* k_cache, const void* v_cache,
-                              const int32_t* block_table, const int32_t* cache_seqlens, void* out,
-                              float* lse_out, int batch, int num_q_heads, int num_kv_heads, int head_dim,
-                              int max_blocks, int64_t q_stride_b, int64_t q_stride_h, int64_t page_stride,
-                              int64_t bt_stride_b, float softmax_scale, int dtype, void* workspace,
-                              size_t workspace_bytes, void* stream, const void* k_new, const void* v_new,
+// Validates the arguments and fills the kernel parameters (shared by every decode entry point).
+static int fill_decode_params(DecodeParams& p, bool& fast_ok, const void* q, const void* k_cache,
+                              const void* v_cache, const int32_t* block_table, const int32_t* cache_seqlens,
+                              void* out, float* lse_out, int batch, int num_q_heads, int num_kv_heads,
+                              int head_dim, int max_blocks, int64_t q_stride_b, int64_t q_stride_h,
+                              int64_t page_stride, int64_t bt_stride_b, float softmax_scale, int dtype,
+                              void* workspace, size_t workspace_bytes, const void* k_new, const void* v_new,
                               int64_t new_stride_b) {
-  clear_error();
   BPKV_CHECK_ARG(batch > 0 && num_q_heads > 0 && head_dim > 0, "page16_native_shape_unsupported:empty");
   BPKV_CHECK_ARG(num_kv_heads > 0 && num_q_heads % num_kv_heads == 0, "page16_native_shape_unsupported:gqa");
   BPKV_CHECK_ARG(head_dim <= 256, "page16_native_shape_unsupported:head_dim_%d", head_dim);
@@ -798,7 +1007,7 @@ static int page16_decode_impl(const void* q, const void* k_cache, const void* v_
     set_error("page16_native_workspace:need_%zu_bytes", w.total);
     return BPKV_ERR_WORKSPACE;
   }
-  DecodeParams p;
+  memset(&p, 0, sizeof(p));
   p.q = q;
   p.k = k_cache;
   p.v = v_cache;
@@ -825,13 +1034,29 @@ static int page16_decode_impl(const void* q, const void* k_cache, const void* v_
   p.k_new = k_new;
   p.v_new = v_new;
   p.new_sb = new_stride_b;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  fast_ok = dtype != BPKV_F32 && (head_dim == 64 || head_dim == 128 || head_dim == 256) && p.n_rep <= 16 &&
+            batch <= 4096 && aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out) &&
+            (q_stride_b % 8 == 0) && (q_stride_h % 8 == 0) && (page_stride % 8 == 0) &&
+            (k_new == nullptr || (aligned16(k_new) && aligned16(v_new) && new_stride_b % 8 == 0));
+  return BPKV_OK;
+}
 
-  const bool fast_ok = dtype != BPKV_F32 && (head_dim == 64 || head_dim == 128 || head_dim == 256) &&
-                       p.n_rep <= 16 && batch <= 4096 && aligned16(q) && aligned16(k_cache) &&
-                       aligned16(v_cache) && aligned16(out) && (q_stride_b % 8 == 0) &&
-                       (q_stride_h % 8 == 0) && (page_stride % 8 == 0) &&
-                       (k_new == nullptr || (aligned16(k_new) && aligned16(v_new) && new_stride_b % 8 == 0));
+static int page16_decode_impl(const void* q, const void* k_cache, const void* v_cache,
+                              const int32_t* block_table, const int32_t* cache_seqlens, void* out,
+                              float* lse_out, int batch, int num_q_heads, int num_kv_heads, int head_dim,
+                              int max_blocks, int64_t q_stride_b, int64_t q_stride_h, int64_t page_stride,
+                              int64_t bt_stride_b, float softmax_scale, int dtype, void* workspace,
+                              size_t workspace_bytes, void* stream, const void* k_new, const void* v_new,
+                              int64_t new_stride_b) {
+  clear_error();
+  DecodeParams p;
+  bool fast_ok = false;
+  const int rc = fill_decode_params(p, fast_ok, q, k_cache, v_cache, block_table, cache_seqlens, out, lse_out,
+                                    batch, num_q_heads, num_kv_heads, head_dim, max_blocks, q_stride_b,
+                                    q_stride_h, page_stride, bt_stride_b, softmax_scale, dtype, workspace,
+                                    workspace_bytes, k_new, v_new, new_stride_b);
+  if (rc != BPKV_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == BPKV_BF16) return dispatch<__nv_bfloat16>(p, st, fast_ok);
   if (dtype == BPKV_F16) return dispatch<__half>(p, st, fast_ok);
   return dispatch<float>(p, st, false);
@@ -987,4 +1212,68 @@ extern "C" BPKV_API int bpkv_page16_decode_noalloc(const void* q, const void* k_
   return bpkv_page16_decode(q, k_cache, v_cache, block_table, cache_seqlens, out, lse_out, batch, num_q_heads,
                             num_kv_heads, head_dim, max_blocks, q_stride_b, q_stride_h, page_stride, bt_stride_b,
                             softmax_scale, dtype, scratch, kNoAllocScratchBytes, stream);
+}
+
+// ---------------------------------------------------------------------------
+// Split-KV decode with the NVLink exchange fused into the combine.
+// ---------------------------------------------------------------------------
+extern "C" BPKV_API int bpkv_split_kv_decode_p2p(const void* q, const void* k_cache, const void* v_cache,
+                                                 const int32_t* block_table, const int32_t* cache_seqlens,
+                                                 void* out, float* lse_out, int batch, int num_q_heads,
+                                                 int num_kv_heads, int head_dim, int max_blocks,
+                                                 int64_t q_stride_b, int64_t q_stride_h, int64_t page_stride,
+                                                 int64_t bt_stride_b, float softmax_scale, int dtype,
+                                                 int out_dtype, void* workspace, size_t workspace_bytes,
+                                                 int num_splits,
+                                                 void* const* peer_bufs, int rank, int world, uint32_t max_polls,
+                                                 int* status, void* stream) {
+  clear_error();
+  BPKV_CHECK_ARG(world >= 1 && world <= peer::kMaxRanks && rank >= 0 && rank < world,
+                 "peer_exchange_shape:rank_%d_of_%d", rank, world);
+  BPKV_CHECK_ARG(head_dim % 4 == 0, "peer_exchange_shape:head_dim_%d", head_dim);
+  BPKV_CHECK_ARG(status != nullptr, "peer_exchange_shape:null_pointer");
+  BPKV_CHECK_ARG(out_dtype == dtype || out_dtype == BPKV_F32, "peer_exchange_shape:out_dtype_%d", out_dtype);
+  BPKV_CHECK_ARG(world == 1 || peer_bufs != nullptr, "peer_exchange_shape:null_pointer");
+  PeerSet ps;
+  memset(&ps, 0, sizeof(ps));
+  for (int r = 0; r < world && world > 1; ++r) {
+    BPKV_CHECK_ARG(peer_bufs[r] != nullptr && aligned16(peer_bufs[r]), "peer_exchange_shape:buffer_%d", r);
+    ps.bufs[r] = static_cast<uint4*>(peer_bufs[r]);
+  }
+  ps.status = status;
+  ps.rank = rank;
+  ps.world = world;
+  ps.max_polls = max_polls;
+  DecodeParams p;
+  bool fast_ok = false;
+  const int rc = fill_decode_params(p, fast_ok, q, k_cache, v_cache, block_table, cache_seqlens, out, lse_out,
+                                    batch, num_q_heads, num_kv_heads, head_dim, max_blocks, q_stride_b,
+                                    q_stride_h, page_stride, bt_stride_b, softmax_scale, dtype, workspace,
+                                    workspace_bytes, nullptr, nullptr, 0);
+  if (rc != BPKV_OK) return rc;
+  p.partials_only = 1;
+  p.num_splits = num_splits;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int G = dispatch_grid(p, fast_ok);
+  int drc;
+  if (dtype == BPKV_BF16) drc = dispatch<__nv_bfloat16>(p, st, fast_ok, false);
+  else if (dtype == BPKV_F16) drc = dispatch<__half>(p, st, fast_ok, false);
+  else drc = dispatch<float>(p, st, false, false);
+  if (drc != BPKV_OK) return drc;
+  const dim3 grid(batch * num_q_heads), block(kCombWarps * 32);
+  const bool f32_out = out_dtype == BPKV_F32;
+  cudaError_t le;
+  if (dtype == BPKV_BF16)
+    le = f32_out ? launch_pdl(split_kv_p2p_kernel<__nv_bfloat16, float>, grid, block, 0, st, p, G, ps)
+                 : launch_pdl(split_kv_p2p_kernel<__nv_bfloat16, __nv_bfloat16>, grid, block, 0, st, p, G, ps);
+  else if (dtype == BPKV_F16)
+    le = f32_out ? launch_pdl(split_kv_p2p_kernel<__half, float>, grid, block, 0, st, p, G, ps)
+                 : launch_pdl(split_kv_p2p_kernel<__half, __half>, grid, block, 0, st, p, G, ps);
+  else
+    le = launch_pdl(split_kv_p2p_kernel<float, float>, grid, block, 0, st, p, G, ps);
+  if (le != cudaSuccess) {
+    set_error("split_kv_decode_p2p_launch:%s", cudaGetErrorString(le));
+    return BPKV_ERR_CUDA;
+  }
+  BPKV_RETURN_LAUNCH("split_kv_decode_p2p_launch");
 }

@@ -1,100 +1,52 @@
-// Split-KV merge over NVLink peer memory, replacing the NCCL all-gather of
-// packed (out, lse) partials + the merge kernel of the long-sequence decode
-// (one sequence whose pages are split across GPUs).
+// Split-KV merge over NVLink peer memory of partials that the caller already
+// holds (one (out, lse) per rank), replacing the NCCL all-gather of packed
+// partials + the merge kernel of the long-sequence decode (one sequence whose
+// pages are split across GPUs).  The exchange buffer and its word format are
+// described in peer_words.cuh; the decode path that produces its own fp32
+// partials and merges them in the same kernel is bpkv_split_kv_decode_p2p
+// (page16_decode.cu).
 //
-// Every rank owns one exchange buffer (cudaMalloc'd by this library, exported
-// to the other processes by CUDA IPC and mapped there once):
-//   uint4  word[2][world][rows][D/2 + 1]   (parity, source rank, row)
-//   uint32 epoch, done                     (local: calls completed, CTAs done)
-// A word carries its own flag: {x0, e, x1, e} holds two fp32 values of the
-// row (out[2j], out[2j+1]; the last word holds lse and 0), each paired with
-// the call number e.  A 16-byte store reaches the peer as 8-byte pieces that
-// each land whole, so a reader that sees e in both flag slots of a word has
-// both of its values: no fence, counter or separate flag is needed, and the
-// exchange costs one NVLink store latency.  Call number e (kept in device
-// memory, so the kernel can be captured in a CUDA graph and replayed) uses
-// parity e & 1: a peer may already write call e+1 while this rank still
-// merges e; e+2 cannot start before this rank has finished e (the peer's
-// call e+1 needed this rank's e+1 words, which come after e).  A stale word
-// holds an older call number, so nothing is ever reset.
-//
-// peer_exchange_kernel<T>, one launch per call, a programmatic dependent
+// peer_exchange_kernel<TP, TO>, one launch per call, a programmatic dependent
 // launch of whatever produced the partial (it waits for that grid first):
 //   CTA c owns rows [8c, 8c+8).  It stores those rows of this rank's partial
-//   (T out converted to fp32, fp32 lse) into every peer's buffer with plain
+//   (TP out converted to fp32, fp32 lse) into every peer's buffer with plain
 //   16-byte stores through the IPC mapping (NVLink), then merges them, one
 //   warp per row: the lse words of every other rank first (bounded spin on
 //   their call number), M = max lse, W = sum exp(lse - M), then out = sum
-//   exp(lse - M) o / W and lse_out = M + log W, each other rank's words read
-//   with the same bounded spin.  The own partial is read in place.  The last
-//   CTA to finish advances the call number.
+//   exp(lse - M) o / W (written as TO) and lse_out = M + log W, each other
+//   rank's words read with the same bounded spin.  The own partial is read in
+//   place.  The last CTA to finish advances the call number.
 // A wait that runs out sets *status = 1 and writes NaN rows; the context stays
 // usable.  No multicast, no TMA: plain loads and stores.
-#include "common.cuh"
+#include "peer_words.cuh"
 
 namespace bpkv {
 namespace {
 
-constexpr int kMaxRanks = 8;
+using peer::kMaxRanks;
 constexpr int kRowsPerCta = 8;  // one merging warp per row
 constexpr int kThreads = kRowsPerCta * 32;
 
 struct PeerArgs {
   uint4* bufs[kMaxRanks];  // every rank's exchange buffer as mapped in this process (own included)
-  const void* part_out;    // [rows][D] this rank's partial output (T)
+  const void* part_out;    // [rows][D] this rank's partial output (TP)
   const float* part_lse;   // [rows] natural-log sum-exp of this rank's partial
-  void* out;               // [rows][D] merged output (T)
+  void* out;               // [rows][D] merged output (TO)
   float* lse_out;          // [rows] or null
   int* status;             // 0 ok, 1 a wait ran out
   int rank, world, rows, D;
   uint32_t max_polls;
 };
 
-__host__ __device__ inline int64_t row_words(int D) { return D / 2 + 1; }
-__host__ __device__ inline int64_t data_words(int world, int rows, int D) { return 2LL * world * rows * row_words(D); }
-__device__ inline uint4* row_ptr(uint4* buf, const PeerArgs& a, int par, int src, int r) {
-  return buf + ((static_cast<int64_t>(par) * a.world + src) * a.rows + r) * row_words(a.D);
-}
-__device__ inline uint32_t* epoch_ptr(uint4* buf, const PeerArgs& a) {
-  return reinterpret_cast<uint32_t*>(buf + data_words(a.world, a.rows, a.D));
-}
-
-__device__ __forceinline__ void st_volatile_v4(uint4* p, uint4 v) {
-  asm volatile("st.volatile.global.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-               : "memory");
-}
-__device__ __forceinline__ uint4 ld_volatile_v4(const uint4* p) {
-  uint4 v;
-  asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ uint64_t now_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Spin until both flag slots of the word hold `epoch`; bounded by the poll budget
-// and by 4 s from t0.  Returns false (and leaves the word undefined) when it ran out.
-__device__ __forceinline__ bool wait_word(const uint4* p, uint32_t epoch, uint32_t& polls, uint32_t max_polls,
-                                          uint64_t t0, uint4& v) {
-  for (;;) {
-    v = ld_volatile_v4(p);
-    if (v.y == epoch && v.w == epoch) return true;
-    if (++polls > max_polls || ((polls & 63u) == 0u && now_ns() - t0 > 4000000000ull)) return false;
-  }
-}
-
-template <typename T>
+template <typename TP, typename TO>
 __global__ void __launch_bounds__(kThreads) peer_exchange_kernel(const __grid_constant__ PeerArgs a) {
   pdl_wait();  // the partial comes from the preceding grid
   uint4* own = a.bufs[a.rank];
-  const uint32_t epoch = *epoch_ptr(own, a) + 1u;  // this call; stored back by the last CTA below
+  const uint32_t epoch = *peer::epoch_ptr(own, a.world, a.rows, a.D) + 1u;  // this call
   const int par = static_cast<int>(epoch & 1u);
-  const int W = static_cast<int>(row_words(a.D)), H = a.D / 2;
+  const int W = static_cast<int>(peer::row_words(a.D)), H = a.D / 2;
   const int r0 = blockIdx.x * kRowsPerCta, r1 = min(a.rows, r0 + kRowsPerCta);
-  const T* src = reinterpret_cast<const T*>(a.part_out);
+  const TP* src = reinterpret_cast<const TP*>(a.part_out);
   // ---- 1. send this CTA's rows to every peer ----
   const int n_words = (r1 - r0) * W;
   for (int e = threadIdx.x; e < (a.world - 1) * n_words; e += blockDim.x) {
@@ -103,23 +55,22 @@ __global__ void __launch_bounds__(kThreads) peer_exchange_kernel(const __grid_co
     const int r = r0 + rem / W, j = rem % W;
     float x0, x1;
     if (j < H) {
-      x0 = Elem<T>::to_f(src[static_cast<int64_t>(r) * a.D + 2 * j]);
-      x1 = Elem<T>::to_f(src[static_cast<int64_t>(r) * a.D + 2 * j + 1]);
+      x0 = Elem<TP>::to_f(src[static_cast<int64_t>(r) * a.D + 2 * j]);
+      x1 = Elem<TP>::to_f(src[static_cast<int64_t>(r) * a.D + 2 * j + 1]);
     } else {
       x0 = a.part_lse[r];
       x1 = 0.f;
     }
-    st_volatile_v4(row_ptr(a.bufs[p], a, par, a.rank, r) + j,
-                   make_uint4(__float_as_uint(x0), epoch, __float_as_uint(x1), epoch));
+    peer::st_word(peer::row_ptr(a.bufs[p], a.world, a.rows, a.D, par, a.rank, r) + j, x0, x1, epoch);
   }
   // ---- 2. merge, one warp per row ----
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = r0 + warp;
   if (r < r1) {
-    T* out = reinterpret_cast<T*>(a.out) + static_cast<int64_t>(r) * a.D;
-    const T* mine = src + static_cast<int64_t>(r) * a.D;
+    TO* out = reinterpret_cast<TO*>(a.out) + static_cast<int64_t>(r) * a.D;
+    const TP* mine = src + static_cast<int64_t>(r) * a.D;
     const float nan = __int_as_float(0x7fc00000);
-    const uint64_t t0 = now_ns();
+    const uint64_t t0 = peer::now_ns();
     uint32_t polls = 0;
     bool ok = true;
     // lane q < world holds rank q's lse
@@ -128,9 +79,9 @@ __global__ void __launch_bounds__(kThreads) peer_exchange_kernel(const __grid_co
       if (lane == a.rank) {
         lq = a.part_lse[r];
       } else {
-        uint4 v;
-        ok = wait_word(row_ptr(own, a, par, lane, r) + H, epoch, polls, a.max_polls, t0, v);
-        lq = __uint_as_float(v.x);
+        float unused;
+        ok = peer::wait_word(peer::row_ptr(own, a.world, a.rows, a.D, par, lane, r) + H, epoch, polls,
+                             a.max_polls, t0, lq, unused);
       }
     }
     float wts[kMaxRanks];
@@ -156,43 +107,46 @@ __global__ void __launch_bounds__(kThreads) peer_exchange_kernel(const __grid_co
           if (q >= a.world || !(wts[q] > 0.f)) continue;
           float v0, v1;
           if (q == a.rank) {
-            v0 = Elem<T>::to_f(mine[2 * j]);
-            v1 = Elem<T>::to_f(mine[2 * j + 1]);
-          } else {
-            uint4 v;
-            if (!wait_word(row_ptr(own, a, par, q, r) + j, epoch, polls, a.max_polls, t0, v)) ok = false;
-            v0 = __uint_as_float(v.x);
-            v1 = __uint_as_float(v.z);
+            v0 = Elem<TP>::to_f(mine[2 * j]);
+            v1 = Elem<TP>::to_f(mine[2 * j + 1]);
+          } else if (!peer::wait_word(peer::row_ptr(own, a.world, a.rows, a.D, par, q, r) + j, epoch, polls,
+                                      a.max_polls, t0, v0, v1)) {
+            ok = false;
+            v0 = v1 = 0.f;
           }
           acc0 += wts[q] * v0;
           acc1 += wts[q] * v1;
         }
-        out[2 * j] = Elem<T>::from_f(acc0 * invW);
-        out[2 * j + 1] = Elem<T>::from_f(acc1 * invW);
+        out[2 * j] = Elem<TO>::from_f(acc0 * invW);
+        out[2 * j + 1] = Elem<TO>::from_f(acc1 * invW);
       }
       all_ok = __all_sync(0xffffffffu, ok);
       if (all_ok && a.lse_out != nullptr && lane == 0) a.lse_out[r] = M + logf(Wsum);
     } else if (all_ok) {  // no rank had keys for this row (the reference's 0/0)
-      for (int d = lane; d < a.D; d += 32) out[d] = Elem<T>::from_f(nan);
+      for (int d = lane; d < a.D; d += 32) out[d] = Elem<TO>::from_f(nan);
       if (a.lse_out != nullptr && lane == 0) a.lse_out[r] = -INFINITY;
     }
     if (!all_ok) {
-      for (int d = lane; d < a.D; d += 32) out[d] = Elem<T>::from_f(nan);
+      for (int d = lane; d < a.D; d += 32) out[d] = Elem<TO>::from_f(nan);
       if (a.lse_out != nullptr && lane == 0) a.lse_out[r] = nan;
       if (lane == 0) atomicExch(a.status, 1);
     }
   }
-  // the last CTA to finish advances the call number for the next call (every
-  // CTA has read it by the time it counts itself done)
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    uint32_t* done = epoch_ptr(own, a) + 1;
-    if (atomicAdd(done, 1u) == gridDim.x - 1) {
-      *done = 0u;
-      *epoch_ptr(own, a) = epoch;
-    }
-  }
+  if (threadIdx.x == 0) peer::finish_call(own, a.world, a.rows, a.D, epoch);
+}
+
+template <typename TP>
+cudaError_t launch_exchange_tp(int out_dtype, dim3 grid, cudaStream_t st, const PeerArgs& a) {
+  if (out_dtype == BPKV_BF16) return launch_pdl(peer_exchange_kernel<TP, __nv_bfloat16>, grid, dim3(kThreads), 0, st, a);
+  if (out_dtype == BPKV_F16) return launch_pdl(peer_exchange_kernel<TP, __half>, grid, dim3(kThreads), 0, st, a);
+  return launch_pdl(peer_exchange_kernel<TP, float>, grid, dim3(kThreads), 0, st, a);
+}
+
+cudaError_t launch_exchange(int dtype, int out_dtype, dim3 grid, cudaStream_t st, const PeerArgs& a) {
+  if (dtype == BPKV_BF16) return launch_exchange_tp<__nv_bfloat16>(out_dtype, grid, st, a);
+  if (dtype == BPKV_F16) return launch_exchange_tp<__half>(out_dtype, grid, st, a);
+  return launch_exchange_tp<float>(out_dtype, grid, st, a);
 }
 
 }  // namespace
@@ -202,7 +156,7 @@ using namespace bpkv;
 
 extern "C" BPKV_API size_t bpkv_peer_exchange_bytes(int world, int rows, int head_dim) {
   if (world <= 0 || world > kMaxRanks || rows <= 0 || head_dim <= 0) return 0;
-  return static_cast<size_t>(data_words(world, rows, head_dim)) * sizeof(uint4) + 4 * sizeof(uint32_t);
+  return peer::exchange_bytes(world, rows, head_dim);
 }
 
 extern "C" BPKV_API int bpkv_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle) {
@@ -258,7 +212,8 @@ extern "C" BPKV_API int bpkv_peer_buffer_free(void* ptr) {
 
 extern "C" BPKV_API int bpkv_split_kv_merge_p2p(const void* part_out, const float* part_lse, void* const* peer_bufs,
                                                 int rank, int world, int rows, int head_dim, uint32_t max_polls,
-                                                void* out, float* lse_out, int* status, int dtype, void* stream) {
+                                                void* out, float* lse_out, int* status, int dtype, int out_dtype,
+                                                void* stream) {
   clear_error();
   BPKV_CHECK_ARG(world >= 1 && world <= kMaxRanks && rank >= 0 && rank < world, "peer_exchange_shape:rank_%d_of_%d",
                  rank, world);
@@ -266,6 +221,8 @@ extern "C" BPKV_API int bpkv_split_kv_merge_p2p(const void* part_out, const floa
                  head_dim);
   BPKV_CHECK_ARG(part_out && part_lse && peer_bufs && out && status, "peer_exchange_shape:null_pointer");
   BPKV_CHECK_ARG(dtype == BPKV_BF16 || dtype == BPKV_F16 || dtype == BPKV_F32, "peer_exchange_shape:dtype");
+  BPKV_CHECK_ARG(out_dtype == BPKV_BF16 || out_dtype == BPKV_F16 || out_dtype == BPKV_F32,
+                 "peer_exchange_shape:out_dtype");
   PeerArgs a;
   memset(&a, 0, sizeof(a));
   for (int r = 0; r < world; ++r) {
@@ -284,10 +241,7 @@ extern "C" BPKV_API int bpkv_split_kv_merge_p2p(const void* part_out, const floa
   a.max_polls = max_polls;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const dim3 grid((rows + kRowsPerCta - 1) / kRowsPerCta);
-  cudaError_t le;
-  if (dtype == BPKV_BF16) le = launch_pdl(peer_exchange_kernel<__nv_bfloat16>, grid, dim3(kThreads), 0, st, a);
-  else if (dtype == BPKV_F16) le = launch_pdl(peer_exchange_kernel<__half>, grid, dim3(kThreads), 0, st, a);
-  else le = launch_pdl(peer_exchange_kernel<float>, grid, dim3(kThreads), 0, st, a);
+  const cudaError_t le = launch_exchange(dtype, out_dtype, grid, st, a);
   if (le != cudaSuccess) {
     set_error("split_kv_merge_p2p_launch:%s", cudaGetErrorString(le));
     return BPKV_ERR_CUDA;

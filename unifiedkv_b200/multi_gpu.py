@@ -72,15 +72,62 @@ def exchange_partials(out_part: torch.Tensor, lse_part: torch.Tensor, group=None
     return gathered[..., :d].contiguous(), gathered[..., d].contiguous()
 
 
+def _split_decode(q, k_cache, v_cache, block_table, cache_seqlens, softmax_scale, n_rep, *, out_dtype,
+                  lse_out=None, num_splits=0, bufs=None, rank=0, world=1, max_polls=0, status=None):
+    """One call of bpkv_split_kv_decode_p2p on the current stream: decode of this
+    rank's page range into fp32 CTA partials, then the fused combine (+ exchange
+    and merge when world > 1).  Returns out [B, h_q, d] in out_dtype."""
+    from .page16_native import _prepare
+    q, block_table, cache_seqlens, (B, hq, hkv, d) = _prepare(q, k_cache, v_cache, block_table, cache_seqlens,
+                                                              n_rep)
+    out = torch.empty((B, hq, d), dtype=out_dtype, device=q.device)
+    if lse_out is not None and (lse_out.dtype != torch.float32 or lse_out.numel() != B * hq
+                                or not lse_out.is_contiguous()):
+        raise RuntimeError("page16_native_shape_unsupported:lse_out")
+    dev = q.device
+    if status is None:
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+    L = _lib.lib()
+    code = _lib.dtype_code(q.dtype)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev)
+        ws = _lib.workspace_for(L.bpkv_page16_decode_workspace_size(B, hq, hkv, d, code), dev, stream, "page16")
+        rc = L.bpkv_split_kv_decode_p2p(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), block_table.data_ptr(), cache_seqlens.data_ptr(),
+            out.data_ptr(), _lib.ptr(lse_out), B, hq, hkv, d, int(block_table.shape[1]),
+            q.stride(0), q.stride(1), k_cache.stride(0), block_table.stride(0), float(softmax_scale), code,
+            _lib.dtype_code(out_dtype), ws.data_ptr(), ws.numel(), int(num_splits), bufs, int(rank), int(world),
+            int(max_polls), status.data_ptr(), stream.cuda_stream)
+    _lib.check(rc, "split_kv_decode_p2p")
+    return out
+
+
+def decode_partial(q, k_cache, v_cache, block_table, cache_seqlens, softmax_scale, n_rep, num_splits=0):
+    """This rank's fp32 partial of a split sequence: (out fp32 [B, h_q, d], lse fp32 [B, h_q]).
+    No rounding to the cache dtype (the NCCL exchange carries it as is)."""
+    B, hq = int(q.shape[0]), int(q.shape[1])
+    lse = torch.empty((B, hq), dtype=torch.float32, device=q.device)
+    out = _split_decode(q, k_cache, v_cache, block_table, cache_seqlens, softmax_scale, n_rep,
+                        out_dtype=torch.float32, lse_out=lse, num_splits=num_splits)
+    return out, lse
+
+
 class PeerMerge:
-    """NVLink peer-memory exchange + merge of split-KV partials (bpkv_split_kv_merge_p2p).
+    """NVLink peer-memory exchange + merge of split-KV partials.
 
     Collective set-up, on every rank of ``group`` with the same ``rows`` and
     ``head_dim``: the library allocates this rank's exchange buffer, the CUDA IPC
     handles travel once over the process group, and the other ranks' buffers are
-    mapped into this process.  Then ``merge`` is called on every rank in the same
-    order; the call count lives in device memory, so merges captured in a CUDA
-    graph replay correctly.  ``close`` (collective) unmaps and frees.
+    mapped into this process.  Then ``decode`` (bpkv_split_kv_decode_p2p: decode,
+    fp32 combine, exchange and merge in two launches) or ``merge``
+    (bpkv_split_kv_merge_p2p, for a partial the caller already holds) is called on
+    every rank in the same order; the call count lives in device memory, so calls
+    captured in a CUDA graph replay correctly.  ``close`` (collective) unmaps and
+    frees.
+
+    A wait for a peer's words that runs out sets a device status word and writes
+    NaN rows; ``check()`` reads the status (a host synchronisation), clears it and
+    raises, and ``check=True`` on a call does that right after it.
     """
 
     def __init__(self, rows: int, head_dim: int, group=None, device: Optional[torch.device] = None,
@@ -116,27 +163,49 @@ class PeerMerge:
         self._bufs = (ctypes.c_void_p * self.world)(*bufs)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
 
+    def decode(self, q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_table: torch.Tensor,
+               cache_seqlens: torch.Tensor, softmax_scale: float, n_rep: int, lse_out: Optional[torch.Tensor] = None,
+               num_splits: int = 0, check: bool = False) -> torch.Tensor:
+        """Split-KV decode of this rank's page range, merged with every other rank's
+        range: q [B, h_q, d] (identical on all ranks, B * h_q == rows) -> [B, h_q, d]
+        in q's dtype, on every rank."""
+        B, hq, d = [int(x) for x in q.shape]
+        if B * hq != self.rows or d != self.head_dim:
+            raise RuntimeError("peer_exchange_shape:decode")
+        out = _split_decode(q, k_cache, v_cache, block_table, cache_seqlens, softmax_scale, n_rep,
+                            out_dtype=q.dtype, lse_out=lse_out, num_splits=num_splits, bufs=self._bufs,
+                            rank=self.rank, world=self.world, max_polls=self.max_polls, status=self.status)
+        if check:
+            self.check()
+        return out
+
     def merge(self, part_out: torch.Tensor, part_lse: torch.Tensor, out_dtype: Optional[torch.dtype] = None,
-              lse_out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """part_out [rows, d] (any of fp32/fp16/bf16, this rank's partial), part_lse fp32 [rows]
-        -> merged [rows, d] in part_out's dtype (out_dtype must match it)."""
+              lse_out: Optional[torch.Tensor] = None, check: bool = False) -> torch.Tensor:
+        """part_out [rows, d] (fp32/fp16/bf16, this rank's partial), part_lse fp32 [rows]
+        -> merged [rows, d] in out_dtype (default: part_out's dtype)."""
         rows, d = int(part_out.shape[0]), int(part_out.shape[1])
-        if rows != self.rows or d != self.head_dim or (out_dtype is not None and out_dtype != part_out.dtype):
+        if rows != self.rows or d != self.head_dim:
             raise RuntimeError("peer_exchange_shape:merge")
+        out_dtype = out_dtype or part_out.dtype
         part_out = part_out.contiguous()
         part_lse = part_lse.reshape(rows).float().contiguous()
-        out = torch.empty_like(part_out)
+        out = torch.empty((rows, d), dtype=out_dtype, device=part_out.device)
         with torch.cuda.device(self.device):
             rc = _lib.lib().bpkv_split_kv_merge_p2p(
                 part_out.data_ptr(), part_lse.data_ptr(), self._bufs, self.rank, self.world, rows, d,
                 self.max_polls, out.data_ptr(), _lib.ptr(lse_out), self.status.data_ptr(),
-                _lib.dtype_code(part_out.dtype), _lib.stream_ptr(self.device))
+                _lib.dtype_code(part_out.dtype), _lib.dtype_code(out_dtype), _lib.stream_ptr(self.device))
         _lib.check(rc, "split_kv_merge_p2p")
+        if check:
+            self.check()
         return out
 
     def check(self) -> None:
-        """Host check of the device status (synchronises): raises if a wait ran out."""
-        if int(self.status.item()) != 0:
+        """Host check of the device status (synchronises): raises if a wait ran out
+        since the last check; the status is cleared either way."""
+        st = int(self.status.item())
+        if st != 0:
+            self.status.zero_()
             raise RuntimeError("peer_exchange_timeout: a rank's partial did not arrive")
 
     def close(self) -> None:
@@ -161,23 +230,26 @@ def _native_merge(parts: torch.Tensor, lses: torch.Tensor, out_dtype: torch.dtyp
 
 def split_kv_decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, local_block_table: torch.Tensor,
                     local_lens: torch.Tensor, softmax_scale: float, n_rep: int, group=None,
-                    merge: Optional[Callable] = None, peer: Optional[PeerMerge] = None) -> torch.Tensor:
+                    merge: Optional[Callable] = None, peer: Optional[PeerMerge] = None,
+                    num_splits: int = 0) -> torch.Tensor:
     """Decode one (or a few) sequences whose pages are split across ranks.
 
     Each rank passes q (identical on all ranks, [B, h_q, d]), its own pool
     view, the block table of ITS page range and the token count in that range.
-    Returns the merged [B, h_q, d] output on every rank.  A rank whose range
-    is empty contributes lse = -inf (nothing).  With ``peer`` (a PeerMerge for
-    rows = B*h_q) the partials travel over NVLink peer memory instead of NCCL.
+    Returns the merged [B, h_q, d] output (q's dtype) on every rank.  A rank
+    whose range is empty contributes lse = -inf (nothing).  Every partial stays
+    fp32 until the final merge.  With ``peer`` (a PeerMerge for rows = B*h_q) the
+    partials travel over NVLink peer memory, combined, exchanged and merged in
+    one kernel after the decode; without it one NCCL all-gather of the packed
+    fp32 partials feeds the merge kernel.
     """
-    from .page16_native import page16_decode_attention
     B, hq, d = [int(x) for x in q.shape]
-    lse = torch.empty((B, hq), dtype=torch.float32, device=q.device)
-    part = page16_decode_attention(q, k_cache, v_cache, local_block_table, local_lens, softmax_scale=softmax_scale,
-                                   n_rep=n_rep, lse_out=lse)
     if peer is not None:
-        return peer.merge(part.reshape(B * hq, d), lse.reshape(B * hq)).reshape(B, hq, d)
-    parts, lses = exchange_partials(part.float().reshape(B * hq, d), lse.reshape(B * hq), group)
+        return peer.decode(q, k_cache, v_cache, local_block_table, local_lens, softmax_scale, n_rep,
+                           num_splits=num_splits)
+    part, lse = decode_partial(q, k_cache, v_cache, local_block_table, local_lens, softmax_scale, n_rep,
+                               num_splits=num_splits)
+    parts, lses = exchange_partials(part.reshape(B * hq, d), lse.reshape(B * hq), group)
     merge = merge or _native_merge
     out, _ = merge(parts, lses, q.dtype)
     return out.reshape(B, hq, d)

@@ -54,6 +54,29 @@ def _page_view_ok(cache: torch.Tensor, num_kv_heads: int, head_dim: int) -> bool
     return s[3] == 1 and s[2] == head_dim and s[1] == num_kv_heads * head_dim
 
 
+def _prepare(q, k_cache, v_cache, block_table, cache_seqlens, n_rep):
+    """Shared validation of the decode entry points (the reference's checks and
+    tokens, core/page16_native.py:100-128): returns q, block_table and
+    cache_seqlens made contiguous int32 / contiguous, and the four sizes."""
+    batch, num_q_heads, num_kv_heads, head_dim = _check_shapes(q, k_cache, v_cache, block_table, cache_seqlens)
+    if int(n_rep) != num_q_heads // num_kv_heads:
+        raise RuntimeError("page16_native_shape_unsupported:gqa")
+    if not (q.is_cuda and k_cache.is_cuda and v_cache.is_cuda and block_table.is_cuda and cache_seqlens.is_cuda):
+        raise RuntimeError("page16_native_unavailable:tensors_not_on_cuda")
+    if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
+        raise RuntimeError("page16_native_shape_unsupported:dtype_mismatch")
+    if not _page_view_ok(k_cache, num_kv_heads, head_dim) or not _page_view_ok(v_cache, num_kv_heads, head_dim):
+        raise RuntimeError("page16_native_shape_unsupported:cache_layout")
+    if k_cache.stride(0) != v_cache.stride(0):
+        raise RuntimeError("page16_native_shape_unsupported:cache_layout")
+    q = q.contiguous()
+    if block_table.dtype != torch.int32:
+        block_table = block_table.to(torch.int32)
+    block_table = block_table.contiguous()
+    cache_seqlens = cache_seqlens.to(dtype=torch.int32).contiguous()
+    return q, block_table, cache_seqlens, (batch, num_q_heads, num_kv_heads, head_dim)
+
+
 def page16_decode_attention(
     q: torch.Tensor,
     k_cache: torch.Tensor,
@@ -89,23 +112,8 @@ def page16_decode_attention(
     replacing the scatter-then-attend pair of direct_forward
     (core/scheduler.py:398-418).
     """
-    batch, num_q_heads, num_kv_heads, head_dim = _check_shapes(q, k_cache, v_cache, block_table, cache_seqlens)
-    if int(n_rep) != num_q_heads // num_kv_heads:
-        raise RuntimeError("page16_native_shape_unsupported:gqa")
-    if not (q.is_cuda and k_cache.is_cuda and v_cache.is_cuda and block_table.is_cuda and cache_seqlens.is_cuda):
-        raise RuntimeError("page16_native_unavailable:tensors_not_on_cuda")
-    if k_cache.dtype != q.dtype or v_cache.dtype != q.dtype:
-        raise RuntimeError("page16_native_shape_unsupported:dtype_mismatch")
-    if not _page_view_ok(k_cache, num_kv_heads, head_dim) or not _page_view_ok(v_cache, num_kv_heads, head_dim):
-        raise RuntimeError("page16_native_shape_unsupported:cache_layout")
-    if k_cache.stride(0) != v_cache.stride(0):
-        raise RuntimeError("page16_native_shape_unsupported:cache_layout")
-
-    q = q.contiguous()
-    if block_table.dtype != torch.int32:
-        block_table = block_table.to(torch.int32)
-    block_table = block_table.contiguous()
-    cache_seqlens = cache_seqlens.to(dtype=torch.int32).contiguous()
+    q, block_table, cache_seqlens, (batch, num_q_heads, num_kv_heads, head_dim) = _prepare(
+        q, k_cache, v_cache, block_table, cache_seqlens, n_rep)
     out = torch.empty_like(q)
     if lse_out is not None:
         if lse_out.dtype != torch.float32 or lse_out.numel() != batch * num_q_heads or not lse_out.is_contiguous():

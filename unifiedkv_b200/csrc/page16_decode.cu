@@ -25,9 +25,12 @@
 //  * Launches.  The combine is a programmatic dependent launch of the decode
 //    grid: it is scheduled during the decode grid's tail (the decode CTAs
 //    signal griddepcontrol.launch_dependents once their work is done) and
-//    waits for the grid's completion before reading the partials.  It signals
-//    its own dependents at its start, so a programmatic dependent of the
-//    combine (the NVLink merge of a split sequence) can become resident early.
+//    waits for the grid's completion before reading the partials.  The decode
+//    grid is itself a programmatic dependent launch (it waits for the previous
+//    grid before touching memory), and the combine signals its dependents at
+//    its start, so the next layer's decode CTAs become resident during the
+//    combine.  A sequence split across GPUs replaces the combine with
+//    split_kv_p2p_kernel (combine + NVLink exchange + merge in one launch).
 //  * Fused append (optional).  With k_new / v_new the warp that owns a
 //    request's last page stores this step's token into the pool and takes its
 //    row from k_new / v_new for the math, so append + decode is one launch.
@@ -145,6 +148,7 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
   constexpr int NT = D / 8;                  // 8-wide output column tiles
 
   int* prefix = reinterpret_cast<int*>(smem + NW * NS * STAGEB);
+  pdl_wait();  // a programmatic dependent launch: the previous grid's writes are visible from here on
   build_prefix(p, prefix);
   const int B = p.B;
   const int64_t total = prefix[B];
@@ -166,9 +170,11 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
   const int g = lane >> 2, cq = lane & 3;
 
   // ---- loader ------------------------------------------------------------
-  auto issue = [&](int64_t fp, int b, int stage) {
+  auto bt_entry = [&](int64_t fp, int b) {
+    return __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + static_cast<int>(fp - prefix[b]));
+  };
+  auto issue = [&](int64_t fp, int b, int page, int stage) {
     const int j = static_cast<int>(fp - prefix[b]);
-    const int page = __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + j);
     const int len_b = eff_len(p, b);
     const int valid_rows = len_b - j * kPage;  // >= 1
     // fused append: this step's token (position len-1) lives in the request's last page; its row
@@ -207,10 +213,17 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
   for (int i = 0; i < NS - 1; ++i) {
     if (ld_p < e) {
       while (prefix[ld_b + 1] <= ld_p) ++ld_b;
-      issue(ld_p, ld_b, i);
+      issue(ld_p, ld_b, bt_entry(ld_p, ld_b), i);
       ++ld_p;
     }
     cp_async_commit();
+  }
+  // the block-table entry of the next page to load is fetched one iteration ahead, so its
+  // latency overlaps the current page's math instead of delaying the next copy
+  int nx_page = 0;
+  if (ld_p < e) {
+    while (prefix[ld_b + 1] <= ld_p) ++ld_b;
+    nx_page = bt_entry(ld_p, ld_b);
   }
 
   // ---- per-request state -------------------------------------------------
@@ -286,9 +299,12 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
   for (int64_t fp = s; fp < e; ++fp) {
     const int it = static_cast<int>(fp - s);
     if (ld_p < e) {
-      while (prefix[ld_b + 1] <= ld_p) ++ld_b;
-      issue(ld_p, ld_b, (it + NS - 1) % NS);
+      issue(ld_p, ld_b, nx_page, (it + NS - 1) % NS);
       ++ld_p;
+      if (ld_p < e) {
+        while (prefix[ld_b + 1] <= ld_p) ++ld_b;
+        nx_page = bt_entry(ld_p, ld_b);
+      }
     }
     cp_async_commit();
 
@@ -404,6 +420,7 @@ template <typename T, int NW>
 __global__ void __launch_bounds__(NW * 32) page16_decode_generic_kernel(DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   int* prefix = reinterpret_cast<int*>(smem);
+  pdl_wait();
   build_prefix(p, prefix);
   const int B = p.B;
   const int64_t total = prefix[B];
@@ -525,37 +542,119 @@ __device__ void lse_merge_row(const float* part_o, const float* part_lse, int64_
   if (lse_out != nullptr && tid == 0) *lse_out = M + logf(W);
 }
 
-// Combine of split requests.  CTA (b, q-head), 8 warps.  The CTAs that own
-// pages of request b are c_lo..c_hi; when every CTA range is non-empty
-// (T >= G) their slots are simply c + b, otherwise (few pages) the empty
-// ranges are skipped with a short serial scan.  Weights exp(lse_i - M) are
-// formed once in shared memory; warp w accumulates parts w, w+8, ... over all
-// head_dim columns (coalesced rows of the partial buffer), then the 8 warp
-// sums are added in a fixed order.  Requests without pages get NaN rows (the
-// reference's 0/0); requests owned by a single CTA were finished by the decode
-// kernel.
+// Combine of split requests.  CTA (b, q-head, 32 head_dim columns), 8 warps.
+// The CTAs that own pages of request b are c_lo..c_hi; when every CTA range is
+// non-empty (T >= G) their slots are simply c + b, otherwise (few pages) the
+// empty ranges are skipped with a short serial scan.  Requests without pages
+// get NaN rows (the reference's 0/0); requests owned by a single CTA were
+// finished by the decode kernel (unless partials_only).
 constexpr int kMaxSlotsPerReq = 1024;  // >= 2 * SM count
 constexpr int kCombWarps = 8;
 
+// Merges the partials of request b (pages first..last-1 of the flattened list),
+// q-head hq, columns d0 + lane.  Call with the whole CTA; on return warp 0 holds
+// o (its lane's column) and lse of the merged row.
+//
+// Latency is what matters here (a few hundred KB from L2), so every load of a
+// batch is issued before any is used: warp w takes slots [32w, 32w + 32) of a
+// batch of 256; lane j loads the lse of slot 32w + j, and lane d loads column
+// d0 + d of all 32 slots' partial rows (32 independent loads in flight per
+// thread).  The warp's max and weights come from shuffles; the 8 warp states
+// (max, weight sum, weighted column sum) are merged in a fixed order.
+__device__ void combine_partials(const DecodeParams& p, int G, int b, int hq, int d0, int64_t first,
+                                 int64_t last, float& o, float& lse) {
+  constexpr int kBatch = kCombWarps * 32;
+  __shared__ int s_slot[kMaxSlotsPerReq];
+  __shared__ int s_n;
+  __shared__ float s_m[kCombWarps], s_l[kCombWarps];
+  __shared__ float s_acc[kCombWarps][32];
+  const int64_t T_ = p.g_prefix[p.B];
+  const int c_lo = owner_of_page(first, T_, G), c_hi = owner_of_page(last - 1, T_, G);
+  const bool dense = T_ >= G;  // every CTA owns >= 1 page
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (!dense) {
+    if (threadIdx.x == 0) {
+      int n = 0;
+      int64_t start = range_start(c_lo, T_, G);
+      for (int c = c_lo; c <= c_hi && n < kMaxSlotsPerReq; ++c) {
+        const int64_t next = range_start(c + 1, T_, G);
+        if (next > start) s_slot[n++] = c + b;
+        start = next;
+      }
+      s_n = n;
+    }
+    __syncthreads();
+  }
+  const int n = dense ? min(c_hi - c_lo + 1, kMaxSlotsPerReq) : s_n;
+  const int d = d0 + lane;
+  const bool dok = d < p.D;
+  auto slot_of = [&](int i) -> int64_t {
+    return dense ? static_cast<int64_t>(c_lo + i + b) : static_cast<int64_t>(s_slot[i]);
+  };
+  float m = -INFINITY, l = 0.f, acc = 0.f;
+  for (int base = 0; base < n; base += kBatch) {
+    const int i0 = base + warp * 32;
+    const int cnt = min(32, n - i0);  // slots of this warp in this batch (warp-uniform, may be <= 0)
+    if (cnt <= 0) continue;
+    const float lj = lane < cnt ? p.part_lse[slot_of(i0 + lane) * p.Hq + hq] : -INFINITY;
+    float v[32];
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      v[k] = (k < cnt && dok) ? p.part_o[(slot_of(i0 + k) * p.Hq + hq) * p.D + d] : 0.f;
+    float mb = lj;
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o2));
+    const float wj = (lj == -INFINITY) ? 0.f : expf(lj - mb);
+    float lb = wj;
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) lb += __shfl_xor_sync(0xffffffffu, lb, o2);
+    float ab = 0.f;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) ab += __shfl_sync(0xffffffffu, wj, k) * v[k];
+    const float mn = fmaxf(m, mb);
+    const float a_old = (m == -INFINITY) ? 0.f : expf(m - mn);
+    const float a_new = (mb == -INFINITY) ? 0.f : expf(mb - mn);
+    l = l * a_old + lb * a_new;
+    acc = acc * a_old + ab * a_new;
+    m = mn;
+  }
+  if (lane == 0) {
+    s_m[warp] = m;
+    s_l[warp] = l;
+  }
+  s_acc[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kCombWarps; ++w) M = fmaxf(M, s_m[w]);
+    float W = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCombWarps; ++w) {
+      if (s_m[w] == -INFINITY) continue;
+      const float e = expf(s_m[w] - M);
+      W += s_l[w] * e;
+      A += s_acc[w][lane] * e;
+    }
+    o = A / W;
+    lse = M + logf(W);
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kCombWarps * 32) page16_decode_combine_kernel(DecodeParams p, int G) {
-  __shared__ int s_slot[kMaxSlotsPerReq];
-  __shared__ float s_w[kMaxSlotsPerReq];
-  __shared__ float s_red[kCombWarps];
-  __shared__ float s_acc[kCombWarps][32];
-  __shared__ int s_n;
   // launched as a programmatic dependent of the decode kernel: wait until that grid has
   // completed and its partials are visible (a no-op for an ordinary launch)
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  // a programmatic dependent (the NVLink merge of a split sequence) may become resident
-  // now; it waits for this grid's completion itself
+  pdl_wait();
+  // the next decode launch (a programmatic dependent) may become resident now; it waits
+  // for this grid's completion itself
   asm volatile("griddepcontrol.launch_dependents;" :::);
   const int b = blockIdx.x, hq = blockIdx.y;
   const int d0 = blockIdx.z * 32;  // this CTA's 32 head_dim columns
-  const int64_t T_ = p.g_prefix[p.B];
-  const int64_t first = p.g_prefix[b], last = p.g_prefix[b + 1];
   const int D = p.D;
   if (d0 >= D) return;
+  const int64_t T_ = p.g_prefix[p.B];
+  const int64_t first = p.g_prefix[b], last = p.g_prefix[b + 1];
   T* ob = reinterpret_cast<T*>(p.out) + (static_cast<int64_t>(b) * p.Hq + hq) * D;
   float* lse_dst = (p.lse_out && blockIdx.z == 0) ? p.lse_out + static_cast<int64_t>(b) * p.Hq + hq : nullptr;
   if (last == first) {
@@ -563,59 +662,13 @@ __global__ void __launch_bounds__(kCombWarps * 32) page16_decode_combine_kernel(
     if (lse_dst != nullptr && threadIdx.x == 0) *lse_dst = -INFINITY;
     return;
   }
-  const int c_lo = owner_of_page(first, T_, G), c_hi = owner_of_page(last - 1, T_, G);
-  if (c_lo == c_hi) return;
-  const bool dense = T_ >= G;  // every CTA owns >= 1 page
-  if (!dense && threadIdx.x == 0) {
-    int n = 0;
-    int64_t start = range_start(c_lo, T_, G);
-    for (int c = c_lo; c <= c_hi && n < kMaxSlotsPerReq; ++c) {
-      const int64_t next = range_start(c + 1, T_, G);
-      if (next > start) s_slot[n++] = c + b;
-      start = next;
-    }
-    s_n = n;
+  if (!p.partials_only && owner_of_page(first, T_, G) == owner_of_page(last - 1, T_, G)) return;
+  float o = 0.f, lse = 0.f;
+  combine_partials(p, G, b, hq, d0, first, last, o, lse);
+  if (threadIdx.x < 32) {
+    if (d0 + threadIdx.x < D) ob[d0 + threadIdx.x] = Elem<T>::from_f(o);
+    if (lse_dst != nullptr && threadIdx.x == 0) *lse_dst = lse;
   }
-  __syncthreads();
-  const int n = dense ? min(c_hi - c_lo + 1, kMaxSlotsPerReq) : s_n;
-  auto slot = [&](int i) { return dense ? (c_lo + i + b) : s_slot[i]; };
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float M = -INFINITY;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) M = fmaxf(M, p.part_lse[static_cast<int64_t>(slot(i)) * p.Hq + hq]);
-  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-  if (lane == 0) s_red[warp] = M;
-  __syncthreads();
-  M = s_red[0];
-  for (int w = 1; w < kCombWarps; ++w) M = fmaxf(M, s_red[w]);
-  __syncthreads();
-  float W = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float w = expf(p.part_lse[static_cast<int64_t>(slot(i)) * p.Hq + hq] - M);
-    s_w[i] = w;
-    W += w;
-  }
-  for (int o = 16; o > 0; o >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o);
-  if (lane == 0) s_red[warp] = W;
-  __syncthreads();
-  W = 0.f;
-  for (int w = 0; w < kCombWarps; ++w) W += s_red[w];
-  // warp-strided accumulation over parts; lane = head_dim column d0 + lane
-  const int d = d0 + lane;
-  float acc = 0.f;
-#pragma unroll 8
-  for (int i = warp; i < n; i += kCombWarps) {
-    const float* po = p.part_o + (static_cast<int64_t>(slot(i)) * p.Hq + hq) * D;
-    if (d < D) acc += s_w[i] * po[d];
-  }
-  s_acc[warp][lane] = acc;
-  __syncthreads();
-  const float inv = 1.f / W;
-  if (threadIdx.x < 32 && d < D) {
-    float a = 0.f;
-    for (int w = 0; w < kCombWarps; ++w) a += s_acc[w][threadIdx.x];
-    ob[d] = Elem<T>::from_f(a * inv);
-  }
-  if (lse_dst != nullptr && threadIdx.x == 0) *lse_dst = M + logf(W);
 }
 
 template <typename T>
@@ -633,18 +686,21 @@ __global__ void lse_combine_kernel(const float* part_o, const float* part_lse, v
 // Split-KV decode of sequences whose pages are split across GPUs: the decode
 // grid (partials_only) leaves one fp32 partial per CTA of every request, and
 // this kernel - a programmatic dependent launch of that grid - does the rest of
-// the layer in one pass per row r = (request b, q-head), one CTA of kCombWarps
-// warps per row:
+// the layer, one CTA of kCombWarps warps per (row r = (request b, q-head),
+// 32 head_dim columns):
 //   1. local combine: the row's CTA partials (fp32, workspace slots) merged by
-//      log-sum-exp into this rank's (o, lse), kept in shared memory in fp32;
-//   2. exchange: (o, lse) stored into every peer's exchange buffer as words
-//      that carry the call number (peer_words.cuh), over NVLink;
-//   3. merge: the peers' words for this row polled from this rank's own buffer
-//      (bounded waits) and merged with the own (o, lse) in fp32, written once as
-//      T (and lse_out).
-// So no partial is ever rounded to T before the final merge, and a layer is two
-// launches (decode, this) instead of three.  With world == 1 steps 2 and 3 are
-// skipped.  A wait that runs out sets *status = 1 and writes a NaN row.
+//      log-sum-exp (combine_partials) into this rank's (o, lse) for the CTA's
+//      columns, kept in fp32;
+//   2. exchange: those columns of (o, lse) stored into every peer's exchange
+//      buffer as words that carry the call number (peer_words.cuh), over NVLink
+//      (the lse word by the column-0 CTA);
+//   3. merge: the peers' lse words and the CTA's data words for this row polled
+//      from this rank's own buffer (bounded waits) and merged with the own
+//      (o, lse) in fp32, written once as TO (and lse_out).
+// So no partial is rounded to a 16-bit type before the final merge, and a layer
+// is two launches (decode, this) instead of three.  With world == 1 steps 2 and
+// 3 reduce to the local combine.  A wait that runs out sets *status = 1 and
+// writes a NaN row.
 // ---------------------------------------------------------------------------
 struct PeerSet {
   uint4* bufs[peer::kMaxRanks];
@@ -656,97 +712,43 @@ struct PeerSet {
 template <typename T, typename TO>
 __global__ void __launch_bounds__(kCombWarps * 32) split_kv_p2p_kernel(DecodeParams p, int G,
                                                                        const __grid_constant__ PeerSet ps) {
-  __shared__ int s_slot[kMaxSlotsPerReq];
-  __shared__ float s_w[kMaxSlotsPerReq];
-  __shared__ float s_red[kCombWarps];
-  __shared__ float s_acc[kCombWarps][256];
-  __shared__ float s_o[256];
+  __shared__ float s_o[32];
+  __shared__ float s_lse;
   __shared__ float s_lq[peer::kMaxRanks];
-  __shared__ int s_n;
   pdl_wait();  // the decode grid's partials and prefix are complete and visible
+  asm volatile("griddepcontrol.launch_dependents;" :::);
   const int r = blockIdx.x, rows = p.B * p.Hq;
   const int b = r / p.Hq, hq = r % p.Hq;
-  const int D = p.D, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t T_ = p.g_prefix[p.B];
+  const int D = p.D, tid = threadIdx.x;
+  const int d0 = blockIdx.y * 32;
   const int64_t first = p.g_prefix[b], last = p.g_prefix[b + 1];
-  // ---- 1. local combine of the CTA partials of request b ----
-  float M = -INFINITY, W = 0.f;
+  // ---- 1. local combine of the CTA partials of request b (this CTA's columns) ----
   if (last > first) {
-    const int c_lo = owner_of_page(first, T_, G), c_hi = owner_of_page(last - 1, T_, G);
-    const bool dense = T_ >= G;
-    if (!dense && tid == 0) {
-      int n = 0;
-      int64_t start = range_start(c_lo, T_, G);
-      for (int c = c_lo; c <= c_hi && n < kMaxSlotsPerReq; ++c) {
-        const int64_t next = range_start(c + 1, T_, G);
-        if (next > start) s_slot[n++] = c + b;
-        start = next;
-      }
-      s_n = n;
-    }
-    __syncthreads();
-    const int n = dense ? min(c_hi - c_lo + 1, kMaxSlotsPerReq) : s_n;
-    auto slot = [&](int i) { return dense ? (c_lo + i + b) : s_slot[i]; };
-    for (int i = tid; i < n; i += blockDim.x) M = fmaxf(M, p.part_lse[static_cast<int64_t>(slot(i)) * p.Hq + hq]);
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    if (lane == 0) s_red[warp] = M;
-    __syncthreads();
-    M = s_red[0];
-    for (int w = 1; w < kCombWarps; ++w) M = fmaxf(M, s_red[w]);
-    __syncthreads();
-    for (int i = tid; i < n; i += blockDim.x) {
-      const float wi = expf(p.part_lse[static_cast<int64_t>(slot(i)) * p.Hq + hq] - M);
-      s_w[i] = wi;
-      W += wi;
-    }
-    for (int o = 16; o > 0; o >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o);
-    if (lane == 0) s_red[warp] = W;
-    __syncthreads();
-    W = 0.f;
-    for (int w = 0; w < kCombWarps; ++w) W += s_red[w];
-    float acc[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-    for (int i = warp; i < n; i += kCombWarps) {
-      const float* po = p.part_o + (static_cast<int64_t>(slot(i)) * p.Hq + hq) * D;
-      const float wi = s_w[i];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int d = lane + 32 * k;
-        if (d < D) acc[k] += wi * po[d];
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int d = lane + 32 * k;
-      if (d < D) s_acc[warp][d] = acc[k];
-    }
-    __syncthreads();
-    const float inv = 1.f / W;
-    for (int d = tid; d < D; d += blockDim.x) {
-      float a = 0.f;
-      for (int w = 0; w < kCombWarps; ++w) a += s_acc[w][d];
-      s_o[d] = a * inv;
-    }
+    float o = 0.f, lse = 0.f;
+    combine_partials(p, G, b, hq, d0, first, last, o, lse);
+    if (tid < 32) s_o[tid] = o;
+    if (tid == 0) s_lse = lse;
   } else {
-    for (int d = tid; d < D; d += blockDim.x) s_o[d] = 0.f;
+    if (tid < 32) s_o[tid] = 0.f;
+    if (tid == 0) s_lse = -INFINITY;
   }
-  const float lse_mine = (W > 0.f) ? M + logf(W) : -INFINITY;
   __syncthreads();
-  // ---- 2. exchange ----
-  const int H = D / 2;
+  const float lse_mine = s_lse;
+  // ---- 2. exchange: words [j0, j1) of the row (+ the lse word from the column-0 CTA) ----
+  const int H = D / 2, j0 = d0 / 2, j1 = min(H, j0 + 16);
+  const int nw = (j1 - j0) + (blockIdx.y == 0 ? 1 : 0);
   uint32_t epoch = 0;
   int par = 0;
   if (ps.world > 1) {
     uint4* own = ps.bufs[ps.rank];
     epoch = *peer::epoch_ptr(own, ps.world, rows, D) + 1u;
     par = static_cast<int>(epoch & 1u);
-    const int nw = H + 1;
     for (int e = tid; e < (ps.world - 1) * nw; e += blockDim.x) {
-      const int i = e / nw, j = e % nw;
+      const int i = e / nw, k = e % nw;
       const int pr = (ps.rank + 1 + i) % ps.world;
-      const float x0 = j < H ? s_o[2 * j] : lse_mine;
-      const float x1 = j < H ? s_o[2 * j + 1] : 0.f;
+      const int j = (k < j1 - j0) ? j0 + k : H;
+      const float x0 = j < H ? s_o[2 * (j - j0)] : lse_mine;
+      const float x1 = j < H ? s_o[2 * (j - j0) + 1] : 0.f;
       peer::st_word(peer::row_ptr(ps.bufs[pr], ps.world, rows, D, par, ps.rank, r) + j, x0, x1, epoch);
     }
   }
@@ -768,45 +770,44 @@ __global__ void __launch_bounds__(kCombWarps * 32) split_kv_p2p_kernel(DecodePar
   const bool failed_lse = __syncthreads_or(!ok);
   float Mg = -INFINITY;
   for (int q = 0; q < ps.world; ++q) Mg = fmaxf(Mg, s_lq[q]);
-  float wq[peer::kMaxRanks], Wg = 0.f;
-#pragma unroll
-  for (int q = 0; q < peer::kMaxRanks; ++q) {
-    wq[q] = (q < ps.world && Mg != -INFINITY) ? expf(s_lq[q] - Mg) : 0.f;
-    Wg += wq[q];
-  }
-  float v0 = 0.f, v1 = 0.f;
-  if (!failed_lse && Mg != -INFINITY && tid < H) {
+  float v0 = 0.f, v1 = 0.f, Wg = 0.f;
+  const int j = j0 + tid;
+  if (!failed_lse && Mg != -INFINITY && tid < 16) {
     for (int q = 0; q < ps.world; ++q) {
-      if (!(wq[q] > 0.f)) continue;
+      const float wq = expf(s_lq[q] - Mg);
+      Wg += wq;
+      if (!(wq > 0.f) || j >= j1) continue;
       float x0, x1;
       if (q == ps.rank) {
         x0 = s_o[2 * tid];
         x1 = s_o[2 * tid + 1];
-      } else if (!peer::wait_word(peer::row_ptr(ps.bufs[ps.rank], ps.world, rows, D, par, q, r) + tid, epoch,
+      } else if (!peer::wait_word(peer::row_ptr(ps.bufs[ps.rank], ps.world, rows, D, par, q, r) + j, epoch,
                                   polls, ps.max_polls, t0, x0, x1)) {
         ok = false;
         x0 = x1 = 0.f;
       }
-      v0 += wq[q] * x0;
-      v1 += wq[q] * x1;
+      v0 += wq * x0;
+      v1 += wq * x1;
     }
   }
   const bool failed = __syncthreads_or(!ok);
   TO* ob = reinterpret_cast<TO*>(p.out) + static_cast<int64_t>(r) * D;
   const float nan = __int_as_float(0x7fc00000);
   if (failed || Mg == -INFINITY) {  // a wait ran out, or no rank had keys for this row (the reference's 0/0)
-    for (int d = tid; d < D; d += blockDim.x) ob[d] = Elem<TO>::from_f(nan);
-    if (tid == 0) {
-      if (p.lse_out != nullptr) p.lse_out[r] = failed ? nan : -INFINITY;
-      if (failed) atomicExch(ps.status, 1);
-    }
+    for (int d = d0 + tid; d < min(D, d0 + 32); d += blockDim.x) ob[d] = Elem<TO>::from_f(nan);
+    if (tid == 0 && blockIdx.y == 0 && p.lse_out != nullptr) p.lse_out[r] = failed ? nan : -INFINITY;
+    if (tid == 0 && failed) atomicExch(ps.status, 1);
   } else {
-    const float invg = 1.f / Wg;
-    if (tid < H) {
-      ob[2 * tid] = Elem<TO>::from_f(v0 * invg);
-      ob[2 * tid + 1] = Elem<TO>::from_f(v1 * invg);
+    if (tid < 16 && j < j1) {
+      const float invg = 1.f / Wg;
+      ob[2 * j] = Elem<TO>::from_f(v0 * invg);
+      ob[2 * j + 1] = Elem<TO>::from_f(v1 * invg);
     }
-    if (tid == 0 && p.lse_out != nullptr) p.lse_out[r] = Mg + logf(Wg);
+    if (tid == 0 && blockIdx.y == 0 && p.lse_out != nullptr) {
+      float W = 0.f;
+      for (int q = 0; q < ps.world; ++q) W += expf(s_lq[q] - Mg);
+      p.lse_out[r] = Mg + logf(W);
+    }
   }
   if (ps.world > 1) {
     __syncthreads();
@@ -906,7 +907,13 @@ int launch_mma(DecodeParams& p, cudaStream_t st, bool combine) {
     set_error("page16_native_launch:smem_attr");
     return BPKV_ERR_CUDA;
   }
-  kern<<<dim3(G, groups), NW * 32, smem, st>>>(p);
+  // a programmatic dependent launch: the CTAs may become resident during the previous grid's
+  // tail (the kernel waits for that grid before touching memory)
+  const cudaError_t dle = launch_pdl(kern, dim3(G, groups), dim3(NW * 32), smem, st, p);
+  if (dle != cudaSuccess) {
+    set_error("page16_native_launch:%s", cudaGetErrorString(dle));
+    return BPKV_ERR_CUDA;
+  }
   if (!combine) BPKV_RETURN_LAUNCH("page16_native_launch");
   // the combine overlaps its launch with the decode grid's tail (programmatic dependent launch)
   cudaLaunchConfig_t cfg = {};
@@ -1260,7 +1267,7 @@ extern "C" BPKV_API int bpkv_split_kv_decode_p2p(const void* q, const void* k_ca
   else if (dtype == BPKV_F16) drc = dispatch<__half>(p, st, fast_ok, false);
   else drc = dispatch<float>(p, st, false, false);
   if (drc != BPKV_OK) return drc;
-  const dim3 grid(batch * num_q_heads), block(kCombWarps * 32);
+  const dim3 grid(batch * num_q_heads, (head_dim + 31) / 32), block(kCombWarps * 32);
   const bool f32_out = out_dtype == BPKV_F32;
   cudaError_t le;
   if (dtype == BPKV_BF16)

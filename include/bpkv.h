@@ -124,7 +124,10 @@ BPKV_API int bpkv_page16_decode_append(const void* q, const void* k_new, const v
  * that loads the library until exit.  Shapes whose scratch
  * (bpkv_page16_decode_workspace_size) exceeds it are rejected with
  * BPKV_ERR_WORKSPACE.  The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress) and should come before any stream capture.
+ * address (cudaGetSymbolAddress) and should come before any stream capture;
+ * the address is kept per device index for the life of the process, so after
+ * cudaDeviceReset (or under another context on that device) it is stale and
+ * this entry point must not be called again there.
  * All calls share the array: calls that overlap on the GPU race and must be
  * serialised by the caller.  It calls no cudaMalloc / cudaFree.
  * ------------------------------------------------------------------------ */

@@ -34,7 +34,9 @@ HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parent.parent))
 from tests.golden.inputs import PAGE16_CASES, checksum, compress_case, page16_case  # noqa: E402
 
-REF = Path(os.environ.get("BPKV_REFERENCE", "/root/reference")) / "core"
+if "BPKV_REFERENCE" not in os.environ:
+    raise SystemExit("set BPKV_REFERENCE to the reference checkout (the directory that holds core/)")
+REF = Path(os.environ["BPKV_REFERENCE"]) / "core"
 sys.path.insert(0, str(REF))
 
 

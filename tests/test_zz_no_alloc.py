@@ -15,6 +15,7 @@ import numpy as np
 import pytest
 import torch
 
+from oracle.page16 import page16_decode_reference
 from tests.golden.inputs import page16_case
 
 pytestmark = pytest.mark.gpu
@@ -61,6 +62,10 @@ def test_noalloc_matches_workspace_entry_point_twice(cuda):
         # 2e-3 decode tolerance (they are in fact bitwise equal)
         assert (out.float() - ref_out.float()).abs().max().item() < 2e-3, call
         assert (lse - ref_lse).abs().max().item() < 1e-3, call
+        # and both against the CPU oracle of the reference's gather-then-attention path
+        o64 = page16_decode_reference(q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy(),
+                                      bt.cpu().numpy(), ln.cpu().numpy(), 1.0 / math.sqrt(d), hq // 8)
+        assert np.abs(out.float().cpu().numpy() - o64).max() < 2e-3, call
 
 
 def test_noalloc_rejects_oversized_scratch(cuda):

@@ -99,6 +99,15 @@ constexpr int kSmemBytes = kGroups * kQBytes + (kNK + kNV) * kKVBytes + 1024 /*a
 // overwrites S_g in place, chunk by chunk: the probabilities of S columns [32c, 32c+32) (tokens
 // 32c..32c+31) go to columns [32c, 32c+16) (hi parts) and [32c+16, 32c+32) (lo parts).
 constexpr uint32_t kTmemCols = 512;
+#ifndef BPKV_PREFILL_SPLIT_P
+#define BPKV_PREFILL_SPLIT_P 1
+#endif
+// bf16 P as hi + lo parts (default: two P.V MMAs per K step, ~16 mantissa bits per
+// probability) or, with -DBPKV_PREFILL_SPLIT_P=0, as one bf16 part.  Measured at config-5
+// shapes the single part runs at 1.3x the throughput, but one bf16 rounding of a weight
+// costs up to 2^-9 relative: rows with few keys or one dominant key then miss the 2e-3
+// max-abs bar (errors up to ~2^-9 |v|), as flash-attn's bf16 P does.
+constexpr bool kSplitPBf16 = BPKV_PREFILL_SPLIT_P != 0;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 256 between rescales
 
 struct __align__(64) TcKernelArgs {
@@ -322,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     auto issue_o = [&](int g, int j) {  // O_g += P_g(j) V(j), P_g from TMEM (bf16: hi part then lo part)
       tc::tc_fence_after();
       const uint64_t vb = dv0 + static_cast<uint64_t>(((j % kNV) * kKVBytes) >> 4);
-      const int parts = kBf16 ? 2 : 1;
+      const int parts = (kBf16 && kSplitPBf16) ? 2 : 1;
       for (int part = 0; part < parts; ++part) {
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
@@ -505,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           sum2[(c >> 1) & 1] = add2(sum2[(c >> 1) & 1], e2);
           float ea, eb;
           up2(e2, ea, eb);
-          if constexpr (kBf16) {
+          if constexpr (kBf16 && kSplitPBf16) {
             // hi = bf16(e), lo = bf16(e - hi); bf16 -> fp32 is a 16-bit shift
             const uint32_t h = pack2<T>(ea, eb);
             const uint64_t l2 = sub2(e2, pk2(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u)));
@@ -520,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         }
         // P_g(it) over this chunk of S_g: token pair per 32-bit column, hi parts then lo parts
         tc::tmem_st16_nowait(ts + c0, hi);
-        if (kBf16) tc::tmem_st16_nowait(ts + c0 + 16, lo);
+        if (kBf16 && kSplitPBf16) tc::tmem_st16_nowait(ts + c0 + 16, lo);
       };
       emit(32, s1);
       {

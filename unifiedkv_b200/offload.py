@@ -88,9 +88,6 @@ class AsyncOffloadManager:
     def _entries(self, seq_id: int) -> List[BlockTableEntry]:
         return [self.page_table[(seq_id, l)] for l in range(self.num_layers) if (seq_id, l) in self.page_table]
 
-    def _mark_resident(self, seq_id: int):
-        pass
-
     def register_sequence(self, seq_id: int, block_ids: List[int], seq_len: int) -> None:
         """Page-table rows for a sequence whose pages (shared by all layers) are already written."""
         with self.lock:
@@ -115,7 +112,6 @@ class AsyncOffloadManager:
                 seq_id=int(seq_id), layer_id=int(layer_id), state=OffloadState.ON_GPU, block_ids=list(block_ids),
                 seq_len=seq_len, logical_seq_len=seq_len, materialized_blocks=len(block_ids),
                 gpu_block_map=list(block_ids), cpu_k_blocks=[None] * n_blocks, cpu_v_blocks=[None] * n_blocks)
-        self._mark_resident(int(seq_id))
         return list(block_ids)
 
     def register_all_layers(self, seq_id: int, block_ids: List[int], seq_len: int, K_list: list, V_list: list,
@@ -136,7 +132,6 @@ class AsyncOffloadManager:
                     seq_len=int(seq_len), logical_seq_len=logical, materialized_blocks=len(block_ids),
                     prefill_anchor_k_mean=anchor, gpu_block_map=list(block_ids),
                     cpu_k_blocks=[None] * len(block_ids), cpu_v_blocks=[None] * len(block_ids))
-        self._mark_resident(int(seq_id))
 
     def _sequence_has_state(self, seq_id: int, state: OffloadState) -> bool:
         return any(e.state == state for e in self._entries(seq_id))

@@ -25,12 +25,10 @@
 //  * Launches.  The combine is a programmatic dependent launch of the decode
 //    grid: it is scheduled during the decode grid's tail (the decode CTAs
 //    signal griddepcontrol.launch_dependents once their work is done) and
-//    waits for the grid's completion before reading the partials.  The decode
-//    grid is itself a programmatic dependent launch (it waits for the previous
-//    grid before touching memory), and the combine signals its dependents at
-//    its start, so the next layer's decode CTAs become resident during the
-//    combine.  A sequence split across GPUs replaces the combine with
-//    split_kv_p2p_kernel (combine + NVLink exchange + merge in one launch).
+//    waits for the grid's completion before reading the partials.  It signals
+//    its own dependents at its start.  A sequence split across GPUs replaces
+//    the combine with split_kv_p2p_kernel (combine + NVLink exchange + merge in
+//    one launch, also a programmatic dependent of the decode grid).
 //  * Fused append (optional).  With k_new / v_new the warp that owns a
 //    request's last page stores this step's token into the pool and takes its
 //    row from k_new / v_new for the math, so append + decode is one launch.
@@ -148,7 +146,6 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
   constexpr int NT = D / 8;                  // 8-wide output column tiles
 
   int* prefix = reinterpret_cast<int*>(smem + NW * NS * STAGEB);
-  pdl_wait();  // a programmatic dependent launch: the previous grid's writes are visible from here on
   build_prefix(p, prefix);
   const int B = p.B;
   const int64_t total = prefix[B];
@@ -170,11 +167,9 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
   const int g = lane >> 2, cq = lane & 3;
 
   // ---- loader ------------------------------------------------------------
-  auto bt_entry = [&](int64_t fp, int b) {
-    return __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + static_cast<int>(fp - prefix[b]));
-  };
-  auto issue = [&](int64_t fp, int b, int page, int stage) {
+  auto issue = [&](int64_t fp, int b, int stage) {
     const int j = static_cast<int>(fp - prefix[b]);
+    const int page = __ldg(p.bt + static_cast<int64_t>(b) * p.bt_sb + j);
     const int len_b = eff_len(p, b);
     const int valid_rows = len_b - j * kPage;  // >= 1
     // fused append: this step's token (position len-1) lives in the request's last page; its row
@@ -213,17 +208,10 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
   for (int i = 0; i < NS - 1; ++i) {
     if (ld_p < e) {
       while (prefix[ld_b + 1] <= ld_p) ++ld_b;
-      issue(ld_p, ld_b, bt_entry(ld_p, ld_b), i);
+      issue(ld_p, ld_b, i);
       ++ld_p;
     }
     cp_async_commit();
-  }
-  // the block-table entry of the next page to load is fetched one iteration ahead, so its
-  // latency overlaps the current page's math instead of delaying the next copy
-  int nx_page = 0;
-  if (ld_p < e) {
-    while (prefix[ld_b + 1] <= ld_p) ++ld_b;
-    nx_page = bt_entry(ld_p, ld_b);
   }
 
   // ---- per-request state -------------------------------------------------
@@ -299,12 +287,9 @@ __global__ void __launch_bounds__(NW * 32, 1) page16_decode_mma_kernel(DecodePar
   for (int64_t fp = s; fp < e; ++fp) {
     const int it = static_cast<int>(fp - s);
     if (ld_p < e) {
-      issue(ld_p, ld_b, nx_page, (it + NS - 1) % NS);
+      while (prefix[ld_b + 1] <= ld_p) ++ld_b;
+      issue(ld_p, ld_b, (it + NS - 1) % NS);
       ++ld_p;
-      if (ld_p < e) {
-        while (prefix[ld_b + 1] <= ld_p) ++ld_b;
-        nx_page = bt_entry(ld_p, ld_b);
-      }
     }
     cp_async_commit();
 
@@ -420,7 +405,6 @@ template <typename T, int NW>
 __global__ void __launch_bounds__(NW * 32) page16_decode_generic_kernel(DecodeParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   int* prefix = reinterpret_cast<int*>(smem);
-  pdl_wait();
   build_prefix(p, prefix);
   const int B = p.B;
   const int64_t total = prefix[B];
@@ -553,90 +537,69 @@ constexpr int kCombWarps = 8;
 
 // Merges the partials of request b (pages first..last-1 of the flattened list),
 // q-head hq, columns d0 + lane.  Call with the whole CTA; on return warp 0 holds
-// o (its lane's column) and lse of the merged row.
-//
-// Latency is what matters here (a few hundred KB from L2), so every load of a
-// batch is issued before any is used: warp w takes slots [32w, 32w + 32) of a
-// batch of 256; lane j loads the lse of slot 32w + j, and lane d loads column
-// d0 + d of all 32 slots' partial rows (32 independent loads in flight per
-// thread).  The warp's max and weights come from shuffles; the 8 warp states
-// (max, weight sum, weighted column sum) are merged in a fixed order.
+// o (its lane's column) and lse of the merged row.  The weights exp(lse_i - M)
+// are formed once in shared memory (M and their sum by block reductions); warp
+// w then accumulates slots w, w+8, ... over its lane's column (coalesced rows
+// of the partial buffer), and the 8 warp sums are added in a fixed order.
+// (Measured against an online log-sum-exp that skips the max pass: this form
+// was faster for the many short combines of a large batch and equal for one
+// long request.)
 __device__ void combine_partials(const DecodeParams& p, int G, int b, int hq, int d0, int64_t first,
                                  int64_t last, float& o, float& lse) {
-  constexpr int kBatch = kCombWarps * 32;
   __shared__ int s_slot[kMaxSlotsPerReq];
-  __shared__ int s_n;
-  __shared__ float s_m[kCombWarps], s_l[kCombWarps];
+  __shared__ float s_w[kMaxSlotsPerReq];
+  __shared__ float s_red[kCombWarps];
   __shared__ float s_acc[kCombWarps][32];
+  __shared__ int s_n;
   const int64_t T_ = p.g_prefix[p.B];
   const int c_lo = owner_of_page(first, T_, G), c_hi = owner_of_page(last - 1, T_, G);
   const bool dense = T_ >= G;  // every CTA owns >= 1 page
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (!dense) {
-    if (threadIdx.x == 0) {
-      int n = 0;
-      int64_t start = range_start(c_lo, T_, G);
-      for (int c = c_lo; c <= c_hi && n < kMaxSlotsPerReq; ++c) {
-        const int64_t next = range_start(c + 1, T_, G);
-        if (next > start) s_slot[n++] = c + b;
-        start = next;
-      }
-      s_n = n;
+  if (!dense && threadIdx.x == 0) {
+    int n = 0;
+    int64_t start = range_start(c_lo, T_, G);
+    for (int c = c_lo; c <= c_hi && n < kMaxSlotsPerReq; ++c) {
+      const int64_t next = range_start(c + 1, T_, G);
+      if (next > start) s_slot[n++] = c + b;
+      start = next;
     }
-    __syncthreads();
+    s_n = n;
   }
+  __syncthreads();
   const int n = dense ? min(c_hi - c_lo + 1, kMaxSlotsPerReq) : s_n;
-  const int d = d0 + lane;
-  const bool dok = d < p.D;
-  auto slot_of = [&](int i) -> int64_t {
-    return dense ? static_cast<int64_t>(c_lo + i + b) : static_cast<int64_t>(s_slot[i]);
-  };
-  float m = -INFINITY, l = 0.f, acc = 0.f;
-  for (int base = 0; base < n; base += kBatch) {
-    const int i0 = base + warp * 32;
-    const int cnt = min(32, n - i0);  // slots of this warp in this batch (warp-uniform, may be <= 0)
-    if (cnt <= 0) continue;
-    const float lj = lane < cnt ? p.part_lse[slot_of(i0 + lane) * p.Hq + hq] : -INFINITY;
-    float v[32];
-#pragma unroll
-    for (int k = 0; k < 32; ++k)
-      v[k] = (k < cnt && dok) ? p.part_o[(slot_of(i0 + k) * p.Hq + hq) * p.D + d] : 0.f;
-    float mb = lj;
-#pragma unroll
-    for (int o2 = 16; o2 > 0; o2 >>= 1) mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, o2));
-    const float wj = (lj == -INFINITY) ? 0.f : expf(lj - mb);
-    float lb = wj;
-#pragma unroll
-    for (int o2 = 16; o2 > 0; o2 >>= 1) lb += __shfl_xor_sync(0xffffffffu, lb, o2);
-    float ab = 0.f;
-#pragma unroll
-    for (int k = 0; k < 32; ++k) ab += __shfl_sync(0xffffffffu, wj, k) * v[k];
-    const float mn = fmaxf(m, mb);
-    const float a_old = (m == -INFINITY) ? 0.f : expf(m - mn);
-    const float a_new = (mb == -INFINITY) ? 0.f : expf(mb - mn);
-    l = l * a_old + lb * a_new;
-    acc = acc * a_old + ab * a_new;
-    m = mn;
+  auto slot = [&](int i) { return dense ? (c_lo + i + b) : s_slot[i]; };
+  float M = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) M = fmaxf(M, p.part_lse[static_cast<int64_t>(slot(i)) * p.Hq + hq]);
+  for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+  if (lane == 0) s_red[warp] = M;
+  __syncthreads();
+  M = s_red[0];
+  for (int w = 1; w < kCombWarps; ++w) M = fmaxf(M, s_red[w]);
+  __syncthreads();
+  float W = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float w = expf(p.part_lse[static_cast<int64_t>(slot(i)) * p.Hq + hq] - M);
+    s_w[i] = w;
+    W += w;
   }
-  if (lane == 0) {
-    s_m[warp] = m;
-    s_l[warp] = l;
+  for (int o2 = 16; o2 > 0; o2 >>= 1) W += __shfl_xor_sync(0xffffffffu, W, o2);
+  if (lane == 0) s_red[warp] = W;
+  __syncthreads();
+  W = 0.f;
+  for (int w = 0; w < kCombWarps; ++w) W += s_red[w];
+  const int d = d0 + lane;
+  float acc = 0.f;
+#pragma unroll 8
+  for (int i = warp; i < n; i += kCombWarps) {
+    const float* po = p.part_o + (static_cast<int64_t>(slot(i)) * p.Hq + hq) * p.D;
+    if (d < p.D) acc += s_w[i] * po[d];
   }
   s_acc[warp][lane] = acc;
   __syncthreads();
   if (warp == 0) {
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kCombWarps; ++w) M = fmaxf(M, s_m[w]);
-    float W = 0.f, A = 0.f;
-#pragma unroll
-    for (int w = 0; w < kCombWarps; ++w) {
-      if (s_m[w] == -INFINITY) continue;
-      const float e = expf(s_m[w] - M);
-      W += s_l[w] * e;
-      A += s_acc[w][lane] * e;
-    }
-    o = A / W;
+    float a = 0.f;
+    for (int w = 0; w < kCombWarps; ++w) a += s_acc[w][lane];
+    o = a / W;
     lse = M + logf(W);
   }
 }
@@ -646,8 +609,8 @@ __global__ void __launch_bounds__(kCombWarps * 32) page16_decode_combine_kernel(
   // launched as a programmatic dependent of the decode kernel: wait until that grid has
   // completed and its partials are visible (a no-op for an ordinary launch)
   pdl_wait();
-  // the next decode launch (a programmatic dependent) may become resident now; it waits
-  // for this grid's completion itself
+  // a programmatic dependent of this grid may become resident now; it waits for this
+  // grid's completion itself
   asm volatile("griddepcontrol.launch_dependents;" :::);
   const int b = blockIdx.x, hq = blockIdx.y;
   const int d0 = blockIdx.z * 32;  // this CTA's 32 head_dim columns
@@ -907,13 +870,9 @@ int launch_mma(DecodeParams& p, cudaStream_t st, bool combine) {
     set_error("page16_native_launch:smem_attr");
     return BPKV_ERR_CUDA;
   }
-  // a programmatic dependent launch: the CTAs may become resident during the previous grid's
-  // tail (the kernel waits for that grid before touching memory)
-  const cudaError_t dle = launch_pdl(kern, dim3(G, groups), dim3(NW * 32), smem, st, p);
-  if (dle != cudaSuccess) {
-    set_error("page16_native_launch:%s", cudaGetErrorString(dle));
-    return BPKV_ERR_CUDA;
-  }
+  // an ordinary launch (measured: as a programmatic dependent of the previous layer's
+  // combine it gained nothing on the batched decode)
+  kern<<<dim3(G, groups), NW * 32, smem, st>>>(p);
   if (!combine) BPKV_RETURN_LAUNCH("page16_native_launch");
   // the combine overlaps its launch with the decode grid's tail (programmatic dependent launch)
   cudaLaunchConfig_t cfg = {};

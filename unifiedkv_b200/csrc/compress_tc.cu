@@ -124,6 +124,10 @@ __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_cons
   const int ntiles_all = (p.Tm + kTok - 1) / kTok;
   const int tile0 = chunk * p.tiles_per_chunk;
   const int ntiles = max(0, min(p.tiles_per_chunk, ntiles_all - tile0));
+  // token tile of step j: pass 2 walks its range backwards, so it starts on the tiles that
+  // pass 1 read last (still in L2: K_mid at 32K tokens is about the size of one die's L2,
+  // and a forward walk would evict each tile just before it is needed)
+  auto tile_of = [&](int j) { return PASS == 2 ? tile0 + ntiles - 1 - j : tile0 + j; };
   auto k_full = [&](int j) { return smem_u32(&bars[j % kNK]); };
   auto k_free = [&](int j) { return smem_u32(&bars[kNK + j % kNK]); };
   auto s_full = [&](int j) { return smem_u32(&bars[2 * kNK + (j & 1)]); };
@@ -179,7 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_cons
         const uint32_t bar = k_full(j);
         mbar_expect_tx(bar, kKBytes);
         uint8_t* dst = ks + (j % kNK) * kKBytes;
-        const int t0 = p.sink + (tile0 + j) * kTok;
+        const int t0 = p.sink + tile_of(j) * kTok;
         tma_load_3d(smem_u32(dst), &args.tmap_k, 0, t0, g, bar);
         tma_load_3d(smem_u32(dst + kTok * 128), &args.tmap_k, 64, t0, g, bar);
       }
@@ -244,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_cons
         tc::tc_fence_after();
         if (mt < mtiles && !failed) {
           const uint32_t tcol = tmem + static_cast<uint32_t>((j & 1) * 256 + mt * 128 + ch * 64) + lane_base;
-          const int nvalid = min(kTok, p.Tm - (tile0 + j) * kTok) - ch * 64;  // valid columns of this half
+          const int nvalid = min(kTok, p.Tm - tile_of(j) * kTok) - ch * 64;  // valid columns of this half
           auto load = [&](int c0, float* a) {
             tc::tmem_ld32(tcol + c0, a);
             if (c0 + 32 > nvalid) {
@@ -355,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1) score_tc_kernel(const __grid_cons
         }
         release(j);
         // each head slot writes its own row; the max over the slots is taken by the block reduction
-        const int t = (tile0 + j) * kTok + tt;
+        const int t = tile_of(j) * kTok + tt;
         if (hs < p.hm_slots && t < p.Tm)
           p.headmax[static_cast<int64_t>(g * p.hm_slots + hs) * p.Tm + t] = failed ? __int_as_float(0x7fc00000) : best;
       }

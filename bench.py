@@ -468,8 +468,8 @@ def run_prefill(args):
     return res
 
 
-PREFILL_P_NOTE = ("; bf16 P is split hi+lo (two P.V MMAs) to stay within 2e-3 of fp64, so the tensor pipe "
-                  "executes 1.5x these FLOPs")
+PREFILL_P_NOTE = ("; bf16 P is split hi+lo (two P.V MMAs) where a tile holds weights above 2^-8 of their rows' "
+                  "running sums, one part elsewhere, so the tensor pipe executes 1.0-1.5x these FLOPs")
 
 
 def cpu_prefill_baseline(past, chunk):

@@ -22,7 +22,9 @@
 //     only when a row max grows by more than 2^8); 1 in 8 exponentials is
 //     evaluated on the FMA pipe by a polynomial to relieve the MUFU unit.  P
 //     is written over S in TMEM as bf16 hi + lo parts (fp16: one part), which
-//     keeps ~16 mantissa bits of each probability for the P.V product.
+//     keeps ~16 mantissa bits of each probability for the P.V product; a tile
+//     whose weights are all small against their rows' running sums (decided
+//     per group and tile) goes as the hi part alone, one P.V MMA instead of two.
 // All waits are bounded; on a timeout the CTA stops, writes NaN rows and
 // still frees its TMEM.  No TMA multicast is used (the loads read this GPU's
 // own pool only).
@@ -108,6 +110,11 @@ constexpr uint32_t kTmemCols = 512;
 // costs up to 2^-9 relative: rows with few keys or one dominant key then miss the 2e-3
 // max-abs bar (errors up to ~2^-9 |v|), as flash-attn's bf16 P does.
 constexpr bool kSplitPBf16 = BPKV_PREFILL_SPLIT_P != 0;
+#ifndef BPKV_PREFILL_LO_LOG2
+#define BPKV_PREFILL_LO_LOG2 8
+#endif
+// a tile skips the lo part when every weight in it is <= 2^-kLoLog2 of its row's running sum
+constexpr float kLoLog2 = BPKV_PREFILL_LO_LOG2;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: P <= 256 between rescales
 
 struct __align__(64) TcKernelArgs {
@@ -177,6 +184,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   static_assert(kBarCount <= 30, "barrier area");
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + kBarCount);
   int* s_fail = reinterpret_cast<int*>(tmem_slot + 1);
+  // per group and tile parity: j + 1 when tile j of the group needs the lo part of P
+  int* s_lo = reinterpret_cast<int*>(bars + 16);
+  static_assert(kBarCount + 1 <= 16, "s_lo follows the barriers, TMEM slot and failure flag");
   int* s_pages = reinterpret_cast<int*>(bars + 32);
   float* s_mx = reinterpret_cast<float*>(s_pages + kMaxPagesSmem);  // [group][2 buffers][kSplit][kBM]
   float* s_l = s_mx + kGroups * 2 * kSplit * kBM;                      // [group][kSplit][kBM]
@@ -245,6 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       tc::mbar_init(o_done(g), 1u);
     }
     *s_fail = 0;
+    for (int i = 0; i < 2 * kGroups; ++i) s_lo[i] = 0;
     tc::fence_mbar_init();
   }
 
@@ -328,10 +339,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       }
       tc::mma_commit(s_full(g));
     };
-    auto issue_o = [&](int g, int j) {  // O_g += P_g(j) V(j), P_g from TMEM (bf16: hi part then lo part)
+    auto issue_o = [&](int g, int j) {  // O_g += P_g(j) V(j), P_g from TMEM (bf16: hi part, then lo part if needed)
       tc::tc_fence_after();
       const uint64_t vb = dv0 + static_cast<uint64_t>(((j % kNV) * kKVBytes) >> 4);
-      const int parts = (kBf16 && kSplitPBf16) ? 2 : 1;
+      // the softmax warps of group g marked tile j (before their p_full arrival) if it needs lo
+      const int parts = (kBf16 && kSplitPBf16 && s_lo[g * 2 + (j & 1)] == j + 1) ? 2 : 1;
       for (int part = 0; part < parts; ++part) {
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk) {
@@ -478,7 +490,32 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       BPKV_MARK(2);
       // exchange the half-row maxima with the partner warp (double-buffered)
       mxg[((it & 1) * kSplit + half) * kBM + row] = mxh;
-      asm volatile("bar.sync %0, %1;\n" ::"r"(bar_id), "n"(32 * kSplit) : "memory");
+      // bf16: can this tile's P go to the P.V MMA as one bf16 part?  Yes when, in every row of
+      // the group, its largest weight is at most 2^-kLoLog2 (2^-8) of the row sum so far
+      // (scale-free: both in units of 2^m_ref; this thread's half-row sum is a lower bound of
+      // the row sum): each weight then keeps a bf16 rounding error <= 2^-9 * 2^-8 of the final
+      // sum, and the random sum of those errors stays far inside the 2e-3 bar.  Measured at
+      // config-5 shapes: 2.4e-4 max-abs against fp64 as with the split everywhere (7.7e-4 with
+      // no split); 2^-6 ran 6% faster but was less accurate than flash-attn's bf16 P on one
+      // chunk.  Otherwise (early tiles, few or dominant keys) the hi/lo split keeps ~16 bits.
+      // One group-wide AND at the max-exchange barrier.
+      bool need_lo = kBf16 && kSplitPBf16;
+      if constexpr (kBf16 && kSplitPBf16) {
+        const float mxh_s = mxh * p.scale_log2;
+        const uint32_t small =
+            (mxh_s == -INFINITY) || (m_ref != -INFINITY && l_run > 0.f && mxh_s - m_ref <= __log2f(l_run) - kLoLog2);
+        uint32_t all_small;
+        asm volatile(
+            "{\n .reg .pred pc, pr;\n setp.ne.u32 pc, %1, 0;\n bar.red.and.pred pr, %2, %3, pc;\n"
+            " selp.u32 %0, 1, 0, pr;\n}\n"
+            : "=r"(all_small)
+            : "r"(small), "r"(10 + g), "n"(32 * kGroupWarps)
+            : "memory");
+        need_lo = all_small == 0;
+        if (need_lo && (warp % kGroupWarps) == 0 && lane == 0) s_lo[g * 2 + (it & 1)] = it + 1;
+      } else {
+        asm volatile("bar.sync %0, %1;\n" ::"r"(bar_id), "n"(32 * kSplit) : "memory");
+      }
       float mxr = mxg[((it & 1) * kSplit) * kBM + row];
 #pragma unroll
       for (int h = 1; h < kSplit; ++h) mxr = fmaxf(mxr, mxg[((it & 1) * kSplit + h) * kBM + row]);
@@ -514,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           sum2[(c >> 1) & 1] = add2(sum2[(c >> 1) & 1], e2);
           float ea, eb;
           up2(e2, ea, eb);
-          if constexpr (kBf16 && kSplitPBf16) {
+          if (kBf16 && kSplitPBf16 && need_lo) {
             // hi = bf16(e), lo = bf16(e - hi); bf16 -> fp32 is a 16-bit shift
             const uint32_t h = pack2<T>(ea, eb);
             const uint64_t l2 = sub2(e2, pk2(__uint_as_float(h << 16), __uint_as_float(h & 0xffff0000u)));
@@ -529,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         }
         // P_g(it) over this chunk of S_g: token pair per 32-bit column, hi parts then lo parts
         tc::tmem_st16_nowait(ts + c0, hi);
-        if (kBf16 && kSplitPBf16) tc::tmem_st16_nowait(ts + c0 + 16, lo);
+        if (kBf16 && kSplitPBf16 && need_lo) tc::tmem_st16_nowait(ts + c0 + 16, lo);
       };
       emit(32, s1);
       {

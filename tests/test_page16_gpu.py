@@ -238,3 +238,45 @@ def test_decode_large_logits(cuda):
     ref = page16_decode_reference(qr, kr, vr, bt, lens, 1 / math.sqrt(128), 4)
     assert np.isfinite(out).all()
     assert _err(out, ref, torch.bfloat16) < 2e-3
+
+
+@pytest.mark.parametrize("hkv,d", [(8, 128), (8, 64), (4, 256)])
+def test_single_request_split_over_ctas(cuda, hkv, d):
+    """Batch 1 (one long request split over every CTA, merged by the combine kernel).
+    Lengths from empty (NaN row, lse -inf) through fewer pages than CTAs (empty CTA
+    ranges) to many pages per CTA; every length twice in a row, with lse_out."""
+    hq = 4 * hkv
+    for L in (0, 1, 17, 100 * 16 + 3, 147 * 16, 148 * 16 + 1, 5000, 40000):
+        for rep in range(2):
+            q, k, v, bt, lens = page16_case(seed=L + rep, batch=1, hq=hq, hkv=hkv, d=d, lens=(L,),
+                                            num_pages=max(4, (L + 15) // 16 + 3), scale_std=0.5)
+            out, lse, (qr, kr, vr) = _run(cuda, q, k, v, bt, lens, torch.bfloat16, lse=True)
+            if L == 0:
+                assert np.isnan(out).all() and np.isneginf(lse).all()
+                continue
+            ref, ref_lse = page16_decode_reference(qr, kr, vr, bt, lens, 1.0 / math.sqrt(d), 4, return_lse=True)
+            assert _err(out, ref, torch.bfloat16) < 2e-3, (L, rep)
+            assert np.abs(lse - ref_lse).max() < 1e-3, (L, rep)
+
+
+def test_single_request_graph_replay(cuda):
+    """The batch-1 decode captured in a CUDA graph and replayed with new lengths
+    (the grid split and the combine follow the lengths on the device)."""
+    from unifiedkv_b200.page16_native import page16_decode_attention
+    q, k, v, bt, lens = page16_case(seed=3, batch=1, hq=32, hkv=8, d=128, lens=(30000,), num_pages=1900,
+                                    scale_std=0.5)
+    tq, tk, tv = (torch.from_numpy(x).to(cuda, torch.bfloat16) for x in (q, k, v))
+    tbt = torch.from_numpy(bt).to(cuda)
+    tl = torch.from_numpy(lens).to(cuda)
+    page16_decode_attention(tq, tk, tv, tbt, tl, softmax_scale=128 ** -0.5, n_rep=4)  # warm (workspace)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = page16_decode_attention(tq, tk, tv, tbt, tl, softmax_scale=128 ** -0.5, n_rep=4)
+    qr, kr, vr = (t.float().cpu().numpy() for t in (tq, tk, tv))
+    for L in (30000, 9, 2371, 30000):
+        tl.fill_(L)
+        g.replay()
+        torch.cuda.synchronize()
+        ref = page16_decode_reference(qr, kr, vr, bt, np.array([L], np.int32), 128 ** -0.5, 4)
+        assert _err(out.float().cpu().numpy(), ref, torch.bfloat16) < 2e-3, L

@@ -81,7 +81,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
         return self
@@ -530,6 +530,11 @@ def run_compress(args):
             sel = topk_blocks(sc, k)
             write_pages(pool_k[l], pool_v[l], Ks[l], Vs[l], dst, sel, k, sink, obs)
     ms = _events_time(step, args.steps, args.warmup)
+
+    def scores_only():
+        for l in range(layers):
+            block_scores(Ks[l], tq, sink, obs, smooth=SMOOTH_ALWAYS, per_kv_head=per_head)
+    ms_scores = _events_time(scores_only, args.steps, args.warmup)
     kmid = 8 * (32768 - sink - obs) * 128 * 2
     bytes_layer = kmid + tq.numel() * 2 + 2 * 2 * eff * 8 * 128 * 2  # K_mid once, Q, retained K+V read+write
     flops_layer = 2 * 2.0 * 32 * 64 * (N * 16) * 128  # QK^T, two passes
@@ -554,9 +559,38 @@ def run_compress(args):
                              f"({tflops / tf:.3f} of measured bf16 burst)"},
         "gpu_launches": 5 * layers * args.steps,  # score pass 1, pass 2, block reduce, top-k, compaction
     }
+    # the scoring passes evaluate one exp2 per (q-head, window row, mid token) each
+    exps_layer = 2.0 * 32 * 64 * (32768 - sink - obs)
+    rate_peak = exp2_rate(dev)
+    rate_scores = exps_layer * layers / (ms_scores * 1e-3)
+    res["exp2"] = {"scoring_us_per_layer": round(ms_scores / layers * 1e3, 2),
+                   "scoring_exp2_per_s": round(rate_scores / 1e12, 4), "measured_peak_exp2_per_s":
+                   round(rate_peak / 1e12, 4), "unit": "T/s", "frac": round(rate_scores / rate_peak, 4),
+                   "note": "exp2 rate of the two scoring passes + block reduction (2*h_q*W*T_mid exponentials per "
+                           "layer, 1 in 8 of them on the FMA pipe) against this GPU's ex2.approx rate measured by "
+                           "bpkv_debug_exp2_rate (independent chains on every SM)"}
     if not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_compress_baseline(K, V, Q, sink, obs, k)
     return res
+
+
+def exp2_rate(dev, iters=4096):
+    """This GPU's hardware exp2 rate (per second), CUDA events around bpkv_debug_exp2_rate."""
+    import torch
+    from unifiedkv_b200 import _lib
+    L = _lib.lib()
+    blocks = 8 * torch.cuda.get_device_properties(dev).multi_processor_count
+    sink = torch.zeros(1, device=dev)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    for _ in range(3):
+        _lib.check(L.bpkv_debug_exp2_rate(blocks, iters, sink.data_ptr(), st), "debug_exp2_rate")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        L.bpkv_debug_exp2_rate(blocks, iters, sink.data_ptr(), st)
+    e1.record()
+    torch.cuda.synchronize()
+    return 5 * L.bpkv_debug_exp2_count(blocks, iters) / (e0.elapsed_time(e1) * 1e-3)
 
 
 def cpu_compress_baseline(K, V, Q, sink, obs, k):

@@ -58,6 +58,14 @@ BPKV_API const char* bpkv_build_hash(void);
 /* Number of streaming multiprocessors of the current device (cached per device). */
 BPKV_API int bpkv_num_sms(void);
 
+/* Diagnostics (no counterpart in the reference): a launch of `blocks` CTAs of 256
+ * threads that evaluate bpkv_debug_exp2_count(blocks, iters) hardware exp2 (the
+ * ex2.approx instruction of the scoring and softmax kernels) in independent
+ * chains; time it with CUDA events to get this GPU's exp2 rate.  sink: any
+ * device float (never written in practice). */
+BPKV_API int bpkv_debug_exp2_rate(int blocks, int iters, float* sink, void* stream);
+BPKV_API long long bpkv_debug_exp2_count(int blocks, int iters);
+
 /* ------------------------------------------------------------------------ *
  * Page16 decode attention.
  * Replaces page16_decode_attention / _page16_decode_kernel

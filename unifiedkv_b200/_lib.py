@@ -31,6 +31,8 @@ SIGNATURES = {
     "bpkv_version": (_c_int, []),
     "bpkv_build_hash": (ctypes.c_char_p, []),
     "bpkv_num_sms": (_c_int, []),
+    "bpkv_debug_exp2_rate": (_c_int, [_c_int, _c_int, _c_p, _c_p]),
+    "bpkv_debug_exp2_count": (ctypes.c_longlong, [_c_int, _c_int]),
     "bpkv_page16_decode_workspace_size": (_c_sz, [_c_int, _c_int, _c_int, _c_int, _c_int]),
     "bpkv_page16_decode": (_c_int, [_c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p,
                                     _c_int, _c_int, _c_int, _c_int, _c_int,

@@ -154,7 +154,10 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
       : "memory");
 }
 
-constexpr int kEmuStride = 8;  // every kEmuStride-th exponential pair goes to the FMA pipe
+#ifndef BPKV_PREFILL_EMU
+#define BPKV_PREFILL_EMU 8
+#endif
+constexpr int kEmuStride = BPKV_PREFILL_EMU;  // every kEmuStride-th exponential pair goes to the FMA pipe
 
 constexpr int kMaxRanked = 512;  // q-tile items ranked per CTA (n^2 / kThreads compares)
 

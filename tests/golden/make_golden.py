@@ -1,14 +1,17 @@
 """Generates the golden fixtures in tests/golden/ from the REFERENCE itself.
 
-Run where the reference tree is mounted (its path from $BPKV_REFERENCE, else the
-build container's mount point below); the fixtures are committed, the reference
-is never read at test time.
+Run where the reference tree is available, with $BPKV_REFERENCE set to it (the
+directory that holds core/); the fixtures are committed, the reference is never
+read at test time.  `python tests/golden/make_golden.py [page16 compress perhead
+score budget writeback]` regenerates the named groups (all by default).
 
   * page16_*.npz  — outputs of the reference Triton kernel ``_page16_decode_kernel``
     (core/page16_native.py:17-80) executed by Triton's CPU interpreter
     (TRITON_INTERPRET=1), on the seeded inputs of tests/golden/inputs.py.
   * compress_*.npz — ``BlockAlignedSnapKV.compress`` (core/compress.py:64-175)
     run unmodified on CPU: retained_block_idx, debug fields, a checksum of K_final.
+  * compress_perhead_*.npz — the same, run once per KV head on that head alone (its
+    K/V and the query heads of its group): the per-KV-head selection mode's golden.
   * score_*.npz — block scores of ``KVScheduler._score_layer_blocks_for_selection``
     (core/scheduler.py:565-592), executed with its hard-coded CUDA device
     redirected to the CPU.
@@ -88,6 +91,36 @@ def gen_compress():
                             k_final_len=int(Kf.shape[2]), debug=json.dumps(dbg),
                             inputs_sha=checksum(K, V, Q), params=json.dumps(spec["params"]), hot=hot)
         print("compress", name, len(idx), Kf.shape)
+
+
+PER_HEAD_CASES = ("ratio_l4100", "hot_l8192")
+
+
+def gen_compress_per_head():
+    """Per-KV-head selection keeps, for KV head h, the blocks that the reference's
+    own BlockAlignedSnapKV.compress keeps when it is given that head alone: K/V
+    head h with the n_rep query heads of its group (repeat_kv maps q-head i to
+    kv-head i // n_rep, core/compress.py:7-20), so the block score is the max over
+    that group's heads only.  One reference call per head."""
+    from compress import BlockAlignedSnapKV
+    for name in PER_HEAD_CASES:
+        spec = COMPRESS_CASES[name]
+        K, V, Q, _ = compress_case(**spec["case"])
+        n_rep = spec["case"]["n_rep"]
+        idx, k_sha, v_sha, lens = [], [], [], []
+        for h in range(K.shape[0]):
+            c = BlockAlignedSnapKV(**spec["params"])
+            Kf, Vf = c.compress(torch.from_numpy(K[h:h + 1])[None], torch.from_numpy(V[h:h + 1])[None],
+                                torch.from_numpy(Q[h * n_rep:(h + 1) * n_rep])[None], n_rep=n_rep)
+            idx.append(np.asarray(c.last_debug["retained_block_idx"][0], np.int64))
+            k_sha.append(checksum(Kf[0].numpy()))
+            v_sha.append(checksum(Vf[0].numpy()))
+            lens.append(int(Kf.shape[2]))
+        np.savez_compressed(HERE / f"compress_perhead_{name}.npz", retained_block_idx=np.stack(idx),
+                            k_final_sha=np.asarray(k_sha), v_final_sha=np.asarray(v_sha),
+                            k_final_len=np.asarray(lens), inputs_sha=checksum(K, V, Q),
+                            params=json.dumps(spec["params"]))
+        print("compress_perhead", name, np.stack(idx).shape)
 
 
 class _CpuTorch(types.ModuleType):
@@ -209,11 +242,13 @@ def gen_writeback():
 
 
 if __name__ == "__main__":
-    which = set(sys.argv[1:]) or {"page16", "compress", "score", "budget", "writeback"}
+    which = set(sys.argv[1:]) or {"page16", "compress", "perhead", "score", "budget", "writeback"}
     if "page16" in which:
         gen_page16()
     if "compress" in which:
         gen_compress()
+    if "perhead" in which:
+        gen_compress_per_head()
     if "score" in which:
         gen_scores()
     if "budget" in which:

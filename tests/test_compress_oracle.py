@@ -117,3 +117,32 @@ def test_per_kv_head_oracle_reduces_to_shared():
         np.testing.assert_array_equal(sel[h], oc.topk_lowest_index(scores[h], sel.shape[1]))
         src = oc.writeback_source_tokens(900, 16, 16, sel[h])
         np.testing.assert_array_equal(Kf[h], np.where(src[:, None] >= 0, K[h, np.maximum(src, 0)], 0))
+
+
+@pytest.mark.parametrize("name", ["ratio_l4100", "hot_l8192"])
+def test_per_kv_head_matches_reference_per_head(name):
+    """Per-KV-head selection pinned to the reference's own code: for KV head h it keeps
+    what BlockAlignedSnapKV.compress keeps when given head h alone with its group's
+    query heads (golden: tests/golden/compress_perhead_*.npz)."""
+    g = np.load(GOLDEN / f"compress_perhead_{name}.npz")
+    K, V, Q, _ = compress_case(**SPECS[name])
+    assert str(g["inputs_sha"]) == checksum(K, V, Q)
+    params = json.loads(str(g["params"]))
+    budget = params.get("retain_budget_tokens", 0)
+    ratio = params.get("retain_ratio", 0.2)
+    sink, obs = params["sink_len"], params["obs_len"]
+    Kf, Vf, sel = oc.compress_per_kv_head(K.astype(np.float64), V.astype(np.float64), Q.astype(np.float64), sink,
+                                          obs, budget, ratio)
+    ref = g["retained_block_idx"]
+    assert sel.shape == ref.shape
+    scores = oc.block_scores(K, Q, sink, obs, per_kv_head=True)
+    for h in range(K.shape[0]):
+        assert Kf.shape[1] == int(g["k_final_len"][h])
+        if np.array_equal(sel[h], ref[h]):
+            assert checksum(Kf[h:h + 1].astype(np.float32)) == str(g["k_final_sha"][h])
+            assert checksum(Vf[h:h + 1].astype(np.float32)) == str(g["v_final_sha"][h])
+            continue
+        # only exact ties at the k-th score may differ (torch.topk's order is unspecified)
+        diff = set(sel[h].tolist()) ^ set(ref[h].tolist())
+        kth = np.sort(scores[h])[::-1][sel.shape[1] - 1]
+        assert all(abs(scores[h][i] - kth) <= 1e-12 * kth for i in diff), (h, diff)

@@ -10,7 +10,10 @@ fallback.
 Pinning: the decode restatement is checked against golden vectors produced by
 the reference's own Triton kernel (run under TRITON_INTERPRET=1), and the
 compression restatement against the reference's own ``BlockAlignedSnapKV``
-(run on CPU); see ``tests/golden/make_golden.py``.  The paged chunked-prefill
-restatement has no reference implementation to pin it (the reference never
-attends chunks over paged KV): parity unpinned for that part.
+(run on CPU, also once per KV head for the per-KV-head mode); see
+``tests/golden/make_golden.py``.  The reference never attends chunks over paged
+KV; its chunk path runs HF ``flash_attention_2`` over a dense cache, so the
+chunked-prefill restatement is pinned on the GPU box instead: the tests compare
+``flash_attn_func`` on the K/V gathered from the pages with this restatement
+(and the build's kernel against both).
 """

@@ -1,7 +1,9 @@
 """Causal chunked-prefill oracle (numpy).  TEST INFRASTRUCTURE ONLY.
 
-Parity unpinned: the reference has no paged chunked-prefill attention (chunks
-run through HF attention over a dense cache, core/engine.py:1772-1854).  This
+The reference has no paged chunked-prefill attention: its chunks run through HF
+flash_attention_2 over a dense cache (core/engine.py:304-305, :1772-1854).  The GPU
+tests pin this restatement to that arithmetic (flash_attn_func on the dense K/V
+gathered from the pages agrees with it within flash-attn's own bf16 error).  This
 restates causal softmax attention with past context, bottom-right aligned as
 flash-attn defines it for seqlen_q <= seqlen_k (query i of an n_q-token chunk
 sees kv tokens t <= seqlen_k - n_q + i), which is also what

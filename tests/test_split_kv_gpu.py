@@ -84,6 +84,28 @@ def test_fused_split_decode_one_rank(cuda, num_splits):
     assert np.abs(lse.cpu().numpy() - ref_lse).max() < 1e-3
 
 
+@pytest.mark.parametrize("hkv,d,dtype", [(8, 64, torch.bfloat16), (4, 256, torch.bfloat16), (8, 128, torch.float16),
+                                         (2, 96, torch.bfloat16)])
+def test_fused_split_decode_head_dims(cuda, hkv, d, dtype):
+    """The fused kernel's 32-column chunks and word ranges for other head sizes (96: the
+    last chunk is partial and the generic decode kernel produces the partials)."""
+    from oracle.page16 import page16_decode_reference
+    from tests.golden.inputs import page16_case
+    from unifiedkv_b200.multi_gpu import _split_decode
+    hq = 4 * hkv
+    q, k, v, bt, lens = page16_case(seed=d, batch=2, hq=hq, hkv=hkv, d=d, lens=(3000, 77), num_pages=260,
+                                    scale_std=0.5)
+    t = [torch.from_numpy(x).to(cuda, dtype) for x in (q, k, v)]
+    lse = torch.empty(2, hq, device=cuda)
+    out = _split_decode(t[0], t[1], t[2], torch.from_numpy(bt).to(cuda), torch.from_numpy(lens).to(cuda),
+                        d ** -0.5, 4, out_dtype=torch.float32, lse_out=lse)
+    torch.cuda.synchronize()
+    ref, ref_lse = page16_decode_reference(*(x.float().cpu().numpy() for x in t), bt, lens, d ** -0.5, 4,
+                                           return_lse=True)
+    assert np.abs(out.cpu().numpy() - ref).max() < 1e-4
+    assert np.abs(lse.cpu().numpy() - ref_lse).max() < 1e-3
+
+
 def test_fused_split_decode_batch_and_empty_rows(cuda):
     """Several requests in one call, one of them without tokens in this range
     (NaN row, lse -inf: the reference's 0/0), with ragged lengths."""

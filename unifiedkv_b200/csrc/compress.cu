@@ -439,35 +439,48 @@ __global__ void page_compact_kernel(const uint8_t* k_src, const uint8_t* v_src, 
   uint8_t* dst = (is_v ? v_pool : k_pool) + static_cast<int64_t>(dst_pages[j]) * page_stride_b;
   const int vec_per_row = row_bytes / static_cast<int>(sizeof(V));
   const int total = kPage * Hkv * vec_per_row;
-  if (vec_per_row <= static_cast<int>(blockDim.x) && blockDim.x % vec_per_row == 0) {
-    // Each thread keeps one column vi of the rows (slot, head) it visits; the source token
-    // is computed once per row, and the loads of a batch of rows go out before its stores.
+  constexpr int kMaxRows = 256;  // (slot, head) rows of one page staged in shared memory
+  if (vec_per_row <= static_cast<int>(blockDim.x) && blockDim.x % vec_per_row == 0 && kPage * Hkv <= kMaxRows) {
+    // The source and destination offsets of each row (slot, head) are computed once, by one
+    // thread, into shared memory (the vec_per_row threads that copy a row's columns would
+    // otherwise each redo the source-token arithmetic); then each thread keeps one column vi
+    // of the rows it visits, and the loads of a batch of rows go out before its stores.
+    __shared__ int64_t s_src[kMaxRows];  // byte offset in src, -1 = zero row, -2 = slot past eff_len
+    __shared__ int64_t s_dst[kMaxRows];
+    const int nrows = kPage * Hkv;
+    for (int rh = threadIdx.x; rh < nrows; rh += blockDim.x) {
+      const int h = rh % Hkv, slot = rh / Hkv;
+      const int p = j * kPage + slot;
+      int64_t so = -2;
+      if (p < eff_len) {  // slots past the compacted length stay untouched
+        const int64_t t = compact_src_token(p, L, sink, obs, kb, selected + h * sel_stride_h);
+        so = t >= 0 ? h * src_sh_b + t * src_st_b : -1;
+      }
+      s_src[rh] = so;
+      s_dst[rh] = slot * dst_st_b + h * dst_sh_b;
+    }
+    __syncthreads();
     constexpr int kBatch = 8;
     const int vi = threadIdx.x % vec_per_row;
     const int rstep = blockDim.x / vec_per_row;
-    const int nrows = kPage * Hkv;
     for (int r0 = threadIdx.x / vec_per_row; r0 < nrows; r0 += rstep * kBatch) {
       V val[kBatch];
-      int64_t doff[kBatch];
+      int64_t so[kBatch];
 #pragma unroll
       for (int u = 0; u < kBatch; ++u) {
         const int rh = r0 + u * rstep;
-        doff[u] = -1;
-        if (rh >= nrows) continue;
-        const int h = rh % Hkv, slot = rh / Hkv;
-        const int p = j * kPage + slot;
-        if (p >= eff_len) continue;  // slots past the compacted length stay untouched
-        const int64_t t = compact_src_token(p, L, sink, obs, kb, selected + h * sel_stride_h);
-        if (t >= 0) {
-          val[u] = __ldg(reinterpret_cast<const V*>(src + h * src_sh_b + t * src_st_b) + vi);
+        so[u] = rh < nrows ? s_src[rh] : -2;
+        if (so[u] >= 0) {
+          val[u] = __ldg(reinterpret_cast<const V*>(src + so[u]) + vi);
         } else {
           memset(&val[u], 0, sizeof(V));
         }
-        doff[u] = slot * dst_st_b + h * dst_sh_b + static_cast<int64_t>(vi) * sizeof(V);
       }
 #pragma unroll
-      for (int u = 0; u < kBatch; ++u)
-        if (doff[u] >= 0) *reinterpret_cast<V*>(dst + doff[u]) = val[u];
+      for (int u = 0; u < kBatch; ++u) {
+        const int rh = r0 + u * rstep;
+        if (so[u] != -2) *(reinterpret_cast<V*>(dst + s_dst[rh]) + vi) = val[u];
+      }
     }
     return;
   }

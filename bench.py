@@ -985,16 +985,26 @@ def run_default(args, rank, world, local_rank):
     _free_cuda()
     extra = argparse.Namespace(**vars(args))
     extra.steps, extra.warmup = max(3, min(args.steps, 10)), max(3, min(args.warmup, 5))
-    sk = run_split_kv(extra, rank, world, local_rank)
-    _free_cuda()
+
+    def guarded(fn, *a):
+        # an extra workload that fails leaves an "error" entry; the headline line is still printed
+        try:
+            return fn(*a)
+        except Exception as exc:  # pragma: no cover - reported in the JSON line
+            import traceback
+            traceback.print_exc(file=sys.stderr)
+            return {"error": f"{type(exc).__name__}: {exc}"[:300]}
+        finally:
+            _free_cuda()
+
+    sk = guarded(run_split_kv, extra, rank, world, local_rank)
     if rank == 0:
         line["split_kv"] = sk
         if world == 1:
             for key, fn in (("compress", run_compress), ("prefill", run_prefill), ("mixed", run_mixed)):
-                line[key] = fn(extra)
-                _free_cuda()
-            line["gpu_launches_extras"] = {k: line[k]["gpu_launches"] for k in ("split_kv", "compress", "prefill",
-                                                                               "mixed")}
+                line[key] = guarded(fn, extra)
+            line["gpu_launches_extras"] = {k: line[k].get("gpu_launches", 0) for k in ("split_kv", "compress",
+                                                                                      "prefill", "mixed")}
         print(json.dumps(line), flush=True)
 
 

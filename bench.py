@@ -965,6 +965,60 @@ def run_mixed_line(args):
     print(json.dumps(run_mixed(args)), flush=True)
 
 
+def run_library_context(args):
+    """Context, not a product path: flashinfer's paged decode (installed library; its NHD paged
+    layout is this pool's [pages, 16, kv_heads, d]) against this build's decode on the same
+    config-2 layers (8 layers of one GPU's 32 requests, each layer its own pool tensors, so
+    nothing is re-read from L2), both timed with CUDA events.  The reference's own Triton
+    kernel cannot run on the GPU box (the reference is not installable), so this is the
+    GPU-to-GPU comparison point."""
+    import torch
+    import flashinfer
+    from unifiedkv_b200.page16_native import page16_decode_attention
+    dev = torch.device("cuda", 0)
+    rng, lens = make_requests(2024)
+    need = (lens + 15) // 16
+    n_pages = int(need.sum()) + 64
+    lay = 8
+    kp = torch.empty((lay, n_pages, 16, HKV, D), dtype=torch.bfloat16, device=dev).normal_(0, 0.5)
+    vp = torch.empty_like(kp).normal_(0, 0.5)
+    perm = rng.permutation(n_pages).astype(np.int32)
+    bt = np.zeros((len(lens), int(need.max())), np.int32)
+    chunks, off = [], 0
+    for b, n in enumerate(need):
+        bt[b, :n] = perm[off:off + n]
+        chunks.append(perm[off:off + n])
+        off += int(n)
+    qs = [(torch.randn(len(lens), HQ, D, device=dev) * 0.5).to(torch.bfloat16) for _ in range(lay)]
+    btd, lnd = torch.from_numpy(bt).to(dev), torch.from_numpy(lens).to(dev)
+    indptr = torch.tensor(np.concatenate([[0], np.cumsum(need)]), dtype=torch.int32, device=dev)
+    idx = torch.tensor(np.concatenate(chunks), dtype=torch.int32, device=dev)
+    last = torch.tensor(lens - (need - 1) * 16, dtype=torch.int32, device=dev)
+    fws = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    bytes_layer = algorithmic_bytes(lens)
+    res = {"metric": "decode KV-read GB/s on config-2 layers: this build vs flashinfer (context)", "unit": "GB/s",
+           "config": {"workload": "8 layers x 32 requests, ctx U[4096,32768], 32q/8kv, d128, bf16, 16-token pages"}}
+    ours = lambda: [page16_decode_attention(qs[l], kp[l], vp[l], btd, lnd, softmax_scale=D ** -0.5,
+                                            n_rep=HQ // HKV) for l in range(lay)]
+    ref_out = ours()[0]
+    ms = _events_time(ours, args.steps, args.warmup) / lay
+    res["this_build_gbs"] = round(bytes_layer / (ms * 1e-3) / 1e9, 1)
+    for tc in (False, True):
+        w = flashinfer.BatchDecodeWithPagedKVCacheWrapper(fws, "NHD", use_tensor_cores=tc)
+        w.plan(indptr, idx, last, HQ, HKV, D, 16, q_data_type=torch.bfloat16, kv_data_type=torch.bfloat16,
+               sm_scale=D ** -0.5)
+        o = w.run(qs[0], (kp[0], vp[0]))
+        ms = _events_time(lambda: [w.run(qs[l], (kp[l], vp[l])) for l in range(lay)], args.steps, args.warmup) / lay
+        key = "flashinfer_tensor_core" if tc else "flashinfer_cuda_core"
+        res[key + "_gbs"] = round(bytes_layer / (ms * 1e-3) / 1e9, 1)
+        res[key + "_max_abs_diff"] = float((o.float() - ref_out.float()).abs().max())
+    res["value"] = res["this_build_gbs"]
+    res["ratio_vs_best_flashinfer"] = round(res["this_build_gbs"] / max(res["flashinfer_tensor_core_gbs"],
+                                                                       res["flashinfer_cuda_core_gbs"]), 3)
+    res["flashinfer_version"] = getattr(flashinfer, "__version__", "?")
+    return res
+
+
 def _free_cuda():
     import gc
     import torch
@@ -1001,10 +1055,12 @@ def run_default(args, rank, world, local_rank):
     if rank == 0:
         line["split_kv"] = sk
         if world == 1:
-            for key, fn in (("compress", run_compress), ("prefill", run_prefill), ("mixed", run_mixed)):
+            for key, fn in (("compress", run_compress), ("prefill", run_prefill), ("mixed", run_mixed),
+                            ("library_context", run_library_context)):
                 line[key] = guarded(fn, extra)
             line["gpu_launches_extras"] = {k: line[k].get("gpu_launches", 0) for k in ("split_kv", "compress",
-                                                                                      "prefill", "mixed")}
+                                                                                      "prefill", "mixed")
+                                           if isinstance(line[k], dict)}
         print(json.dumps(line), flush=True)
 
 
@@ -1014,7 +1070,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill", "compress", "longseq", "mixed"],
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "compress", "longseq", "mixed", "library"],
                     help="decode = headline config 2; the others print their own metric line")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
@@ -1045,7 +1102,8 @@ def main():
         elif args.workload == "longseq":
             run_longseq(args, rank, world, local_rank)
         elif rank == 0:
-            {"prefill": run_prefill_line, "compress": run_compress_line, "mixed": run_mixed_line}[args.workload](args)
+            {"prefill": run_prefill_line, "compress": run_compress_line, "mixed": run_mixed_line,
+             "library": lambda a: print(json.dumps(run_library_context(a)), flush=True)}[args.workload](args)
     finally:
         if world > 1:
             import torch.distributed as dist

@@ -1019,6 +1019,60 @@ def run_library_context(args):
     return res
 
 
+def run_library_prefill_context(args):
+    """Context, not a product path: flashinfer's paged prefill (its FA2 and trtllm-gen backends,
+    page size 16, causal) against this build's chunked prefill on the config-5 prefill part
+    (8 layers, each with its own pool tensors), CUDA events."""
+    import torch
+    import flashinfer
+    from unifiedkv_b200.chunked_prefill import paged_chunk_prefill
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(55)
+    nreq, chunk, lay = 8, 512, 8
+    past = np.clip(np.exp(rng.normal(np.log(4000), 0.8, size=nreq)), 256, 32768).astype(np.int64)
+    totals = past + chunk
+    need = (totals + 15) // 16
+    n_pages = int(need.sum()) + 16
+    kp = torch.empty((lay, n_pages, 16, HKV, D), dtype=torch.bfloat16, device=dev).normal_(0, 0.5)
+    vp = torch.empty_like(kp).normal_(0, 0.5)
+    perm = rng.permutation(n_pages).astype(np.int32)
+    bt = np.zeros((nreq, int(need.max())), np.int32)
+    chunks, off = [], 0
+    for b, n in enumerate(need):
+        bt[b, :n] = perm[off:off + n]
+        chunks.append(perm[off:off + n])
+        off += int(n)
+    bt_d = torch.from_numpy(bt).to(dev)
+    cu = torch.tensor(np.concatenate([[0], np.cumsum([chunk] * nreq)]), dtype=torch.int32, device=dev)
+    sk = torch.tensor(totals, dtype=torch.int32, device=dev)
+    qs = [(torch.randn(nreq * chunk, HQ, D, device=dev) * 0.5).to(torch.bfloat16) for _ in range(lay)]
+    flops = 4.0 * HQ * D * float(np.sum(chunk * (past + (chunk + 1) / 2.0)))
+    ours = lambda: [paged_chunk_prefill(qs[l], kp[l], vp[l], bt_d, None, None, D ** -0.5, HQ // HKV, cu_seqlens_q=cu,
+                                        seqlens_k=sk, max_seqlen_q=chunk) for l in range(lay)]
+    ref_out = ours()[0]
+    ms = _events_time(ours, args.steps, args.warmup) / lay
+    res = {"metric": "paged chunked-prefill TFLOP/s on config-5 chunks: this build vs flashinfer (context)",
+           "unit": "TFLOP/s", "this_build_tflops": round(flops / (ms * 1e-3) / 1e12, 1)}
+    indptr = torch.tensor(np.concatenate([[0], np.cumsum(need)]), dtype=torch.int32, device=dev)
+    idx = torch.tensor(np.concatenate(chunks), dtype=torch.int32, device=dev)
+    last = torch.tensor(totals - (need - 1) * 16, dtype=torch.int32, device=dev)
+    fws = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    for backend in ("fa2", "trtllm-gen"):
+        try:
+            w = flashinfer.BatchPrefillWithPagedKVCacheWrapper(fws, "NHD", backend=backend)
+            w.plan(cu, indptr, idx, last, HQ, HKV, D, 16, causal=True, sm_scale=D ** -0.5, q_data_type=torch.bfloat16,
+                   kv_data_type=torch.bfloat16)
+            o = w.run(qs[0], (kp[0], vp[0]))
+            ms = _events_time(lambda: [w.run(qs[l], (kp[l], vp[l])) for l in range(lay)], args.steps,
+                              args.warmup) / lay
+            res[f"flashinfer_{backend}_tflops"] = round(flops / (ms * 1e-3) / 1e12, 1)
+            res[f"flashinfer_{backend}_max_abs_diff"] = float((o.float() - ref_out.float()).abs().max())
+        except Exception as exc:  # pragma: no cover - a backend this box cannot run
+            res[f"flashinfer_{backend}"] = f"unavailable: {type(exc).__name__}"
+    res["value"] = res["this_build_tflops"]
+    return res
+
+
 def _free_cuda():
     import gc
     import torch
@@ -1103,7 +1157,8 @@ def main():
             run_longseq(args, rank, world, local_rank)
         elif rank == 0:
             {"prefill": run_prefill_line, "compress": run_compress_line, "mixed": run_mixed_line,
-             "library": lambda a: print(json.dumps(run_library_context(a)), flush=True)}[args.workload](args)
+             "library": lambda a: [print(json.dumps(fn(a)), flush=True)
+                                   for fn in (run_library_context, run_library_prefill_context)]}[args.workload](args)
     finally:
         if world > 1:
             import torch.distributed as dist
